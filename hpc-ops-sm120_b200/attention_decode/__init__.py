@@ -1,0 +1,230 @@
+"""BF16 split-K attention decode for NVIDIA B200 (sm_100a).
+
+Drop-in for the reference package's entry point
+``attention_decode(q, k, v)`` (attention_decode/__init__.py:26-39): same
+argument meaning, tensor layouts and error behaviour, with two compatible
+extensions -- an optional per-sequence ``seqlens`` and head groups of 8.
+
+Q: [B, Hq, 1, D]; K, V: [B, Hkv, S, D]; all BF16, contiguous, on one CUDA
+device.  D is 64 or 128 and Hq / Hkv is 1, 4 or 8.  Work is enqueued on the
+current CUDA stream with no host synchronisation, so calls can be captured in
+CUDA graphs.  The kernels live in libattention_decode_b200.so (C ABI,
+include/attention_decode_b200.h); there is no CPU or PyTorch fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from functools import lru_cache
+
+from . import _lib
+from ._lib import AttentionDecodeError
+
+__all__ = [
+    "attention_decode",
+    "attention_decode_partial",
+    "combine_partials",
+    "workspace_bytes",
+    "read_error_flag",
+    "AttentionDecodeError",
+]
+
+_GROUPS = (1, 4, 8)
+_DIMS = (64, 128)
+_ws_cache: dict = {}
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _fail(message: str):
+    # The reference raises these from TORCH_CHECK (c10::Error -> RuntimeError),
+    # csrc/decode.cu:225-244.
+    raise RuntimeError(message)
+
+
+def _validate(q, k, v, seqlens=None):
+    """Mirror of the reference's checks (attention_decode/__init__.py:35-38
+    and csrc/decode.cu:225-241), with the INT_MAX size limit dropped (64-bit
+    indexing) and G = 8 accepted."""
+    torch = _torch()
+    if not all(isinstance(x, torch.Tensor) for x in (q, k, v)):
+        raise TypeError("Q, K, and V must be tensors")
+    if not all(x.is_cuda for x in (q, k, v)):
+        raise ValueError("Q, K, and V must be CUDA tensors")
+    for x in (q, k, v):
+        if x.dtype != torch.bfloat16:
+            _fail("Q/K/V dtype must be BF16 (bfloat16)")
+        if x.dim() != 4:
+            _fail("Q/K/V must have rank four")
+        if not x.is_contiguous():
+            _fail("Q/K/V must be contiguous")
+        if x.requires_grad:
+            _fail("attention_decode is forward inference only; no backward/grad support")
+        if x.numel() == 0:
+            _fail("empty tensors are unsupported")
+    if q.device != k.device or q.device != v.device:
+        _fail("Q/K/V device must match")
+    if k.shape != v.shape:
+        _fail("K/V shape must match")
+    if q.shape[2] != 1:
+        _fail("query length must be 1")
+    if q.shape[0] != k.shape[0] or q.shape[3] != k.shape[3]:
+        _fail("Q/K/V batch and head dimension must match")
+    if q.shape[1] % k.shape[1] != 0:
+        _fail("query heads must be divisible by KV heads")
+    group = q.shape[1] // k.shape[1]
+    if group not in _GROUPS:
+        _fail("supported GQA group sizes are 1, 4 and 8")
+    if q.shape[3] not in _DIMS:
+        _fail("head dimension must be 64 or 128")
+    if seqlens is not None:
+        if not isinstance(seqlens, torch.Tensor):
+            raise TypeError("seqlens must be a tensor")
+        if seqlens.device != q.device:
+            _fail("seqlens must be on the same CUDA device as Q/K/V")
+        if seqlens.dtype != torch.int32:
+            _fail("seqlens dtype must be int32")
+        if seqlens.dim() != 1 or seqlens.shape[0] != q.shape[0] or not seqlens.is_contiguous():
+            _fail("seqlens must be a contiguous [batch] tensor")
+
+
+def workspace_bytes(batch, q_heads, kv_heads, kv_len, head_dim, has_seqlens=False, device=0) -> int:
+    """Device workspace one decode call needs (adb_decode_workspace_size)."""
+    key = (batch, q_heads, kv_heads, kv_len, head_dim, bool(has_seqlens), device)
+    cached = _ws_cache.get(key)
+    if cached is not None:
+        return cached
+    lib = _lib.load_library()
+    out = ctypes.c_size_t(0)
+    _lib.check(
+        lib,
+        lib.adb_decode_workspace_size(
+            batch, q_heads, kv_heads, kv_len, head_dim, int(bool(has_seqlens)), device, ctypes.byref(out)
+        ),
+    )
+    _ws_cache[key] = out.value
+    return out.value
+
+
+def _launch(q, k, v, seqlens, out=None, acc=None, ml=None):
+    torch = _torch()
+    lib = _lib.load_library()
+    batch, q_heads, _, head_dim = q.shape
+    kv_heads, kv_len = k.shape[1], k.shape[2]
+    device = q.device.index if q.device.index is not None else torch.cuda.current_device()
+    nbytes = workspace_bytes(batch, q_heads, kv_heads, kv_len, head_dim, seqlens is not None, device)
+    # Stream-ordered scratch from the caching allocator: safe under CUDA graphs
+    # and concurrent streams (reference: at::empty partial, csrc/decode.cu:205).
+    workspace = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=q.device)
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    lens = seqlens.data_ptr() if seqlens is not None else None
+    if out is not None:
+        status = lib.adb_decode(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), lens, out.data_ptr(),
+            batch, q_heads, kv_heads, kv_len, head_dim,
+            workspace.data_ptr(), workspace.numel(), device, stream,
+        )
+    else:
+        status = lib.adb_decode_partial(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), lens, acc.data_ptr(), ml.data_ptr(),
+            batch, q_heads, kv_heads, kv_len, head_dim,
+            workspace.data_ptr(), workspace.numel(), device, stream,
+        )
+    _lib.check(lib, status)
+
+
+def attention_decode(q, k, v, seqlens=None):
+    """Forward-only single-query attention for contiguous BF16 CUDA tensors.
+
+    Q: [B,Hq,1,D], K/V: [B,Hkv,S,D].  D is 64 or 128 and Hq/Hkv is 1, 4 or
+    8.  ``seqlens`` (optional int32 [B] CUDA tensor) restricts sequence b to
+    its first seqlens[b] tokens of the padded cache; a length of 0 gives a
+    zero row.  Returns a new [B,Hq,1,D] BF16 tensor.  Uses the current CUDA
+    stream.
+    """
+    _validate(q, k, v, seqlens)
+    out = _torch().empty(q.shape, dtype=q.dtype, device=q.device)
+    _launch(q, k, v, seqlens, out=out)
+    return out
+
+
+def attention_decode_partial(q, k, v, seqlens=None, *, out_acc=None, out_ml=None):
+    """Unnormalised decode state over this call's KV, for sequence sharding.
+
+    Returns ``(acc, ml)``: acc FP32 [B, Hq, D] = sum_t exp(s_t - m) V_t and ml
+    FP32 [B, Hq, 2] = (m, l) with m the max logit (natural units) and
+    l = sum_t exp(s_t - m).  ``out_acc``/``out_ml`` may supply contiguous
+    FP32 buffers of those shapes.  Merge states with :func:`combine_partials`.
+    """
+    torch = _torch()
+    _validate(q, k, v, seqlens)
+    batch, q_heads, _, head_dim = q.shape
+    acc = out_acc if out_acc is not None else torch.empty((batch, q_heads, head_dim), dtype=torch.float32, device=q.device)
+    ml = out_ml if out_ml is not None else torch.empty((batch, q_heads, 2), dtype=torch.float32, device=q.device)
+    for buf, shape in ((acc, (batch, q_heads, head_dim)), (ml, (batch, q_heads, 2))):
+        if tuple(buf.shape) != shape or buf.dtype != torch.float32 or not buf.is_contiguous() or buf.device != q.device:
+            _fail(f"partial-state buffers must be contiguous float32 {shape} on {q.device}")
+    _launch(q, k, v, seqlens, acc=acc, ml=ml)
+    return acc, ml
+
+
+def combine_partials(acc, ml, out=None):
+    """Merge R partial states into a BF16 output.
+
+    ``acc`` FP32 [R, rows, D] and ``ml`` FP32 [R, rows, 2], each with
+    contiguous rows inside a part and any stride between parts (so views into
+    an all-gathered buffer work).  Returns BF16 [rows, D] (or writes ``out``).
+    """
+    torch = _torch()
+    lib = _lib.load_library()
+    if acc.dtype != torch.float32 or ml.dtype != torch.float32:
+        _fail("partial states must be float32")
+    if not (acc.is_cuda and ml.is_cuda):
+        raise ValueError("partial states must be CUDA tensors")
+    parts, rows, head_dim = acc.shape
+    if tuple(ml.shape) != (parts, rows, 2):
+        _fail("ml must have shape [parts, rows, 2]")
+    if acc.stride(1) != head_dim or acc.stride(2) != 1 or ml.stride(1) != 2 or ml.stride(2) != 1:
+        _fail("partial states must have contiguous rows")
+    if out is None:
+        out = torch.empty((rows, head_dim), dtype=torch.bfloat16, device=acc.device)
+    elif out.dtype != torch.bfloat16 or not out.is_contiguous() or out.numel() != rows * head_dim:
+        _fail("out must be a contiguous bf16 buffer of rows * head_dim elements")
+    device = acc.device.index if acc.device.index is not None else torch.cuda.current_device()
+    stream = torch.cuda.current_stream(acc.device).cuda_stream
+    _lib.check(
+        lib,
+        lib.adb_combine(
+            acc.data_ptr(), acc.stride(0), ml.data_ptr(), ml.stride(0), parts, rows, head_dim,
+            out.data_ptr(), device, stream,
+        ),
+    )
+    return out
+
+
+def read_error_flag(device=0, reset=True) -> int:
+    """Sticky device error word (non-zero if a kernel's bounded wait expired)."""
+    lib = _lib.load_library()
+    flag = ctypes.c_int(0)
+    _lib.check(lib, lib.adb_read_error_flag(device, ctypes.byref(flag), int(bool(reset))))
+    return flag.value
+
+
+class _Extension:
+    """Object with the reference extension's ``forward(q, k, v)`` method
+    (csrc/binding.cpp:6-8), so code that calls ``_get_extension().forward``
+    keeps working."""
+
+    @staticmethod
+    def forward(q, k, v):
+        return attention_decode(q, k, v)
+
+
+@lru_cache(maxsize=1)
+def _get_extension():
+    _lib.load_library()
+    return _Extension()

@@ -1,0 +1,528 @@
+// decode_capi.cu -- host side of libattention_decode_b200.so: argument
+// checks, the split plan, TMA descriptor encoding, kernel launches and the
+// extern "C" entry points declared in include/attention_decode_b200.h.
+//
+// The reference does all of this inside attention_decode_cuda
+// (csrc/decode.cu:193-258) with ATen types; here the boundary takes plain
+// pointers and sizes, the caller owns every buffer (output and workspace),
+// and nothing synchronises the host.
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <atomic>
+#include <mutex>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "attention_decode_b200.h"
+#include "decode_kernels.cuh"
+
+namespace {
+
+thread_local std::string t_last_error;
+std::atomic<int64_t> g_launches{0};
+
+// Per-thread diagnostic timing of the streaming kernel (adb_timing_*).
+struct Timing {
+  bool enabled = false;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> events;
+};
+thread_local Timing t_timing;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(ADB_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+// ------------------------------------------------------------ kernel table
+struct Variant {
+  const char* name;
+  int head_dim;
+  int tile_tokens;
+  int threads;
+  int smem_bytes;
+  bool tma;
+  const void* fn;
+};
+
+template <int D, int W, int MB, int ST, bool TMA>
+constexpr Variant make_variant(const char* name) {
+  using C = adb::StreamCfg<D, W, MB, ST, TMA>;
+  return Variant{name,     D,   C::kTT, C::kThreads, C::kSmemBytes,
+                 TMA,      reinterpret_cast<const void*>(&adb::decode_stream_kernel<D, W, MB, ST, TMA>)};
+}
+
+// Name format: d<head_dim>_<tma|generic>_tt<tile tokens>_s<stages>.
+const Variant kVariants[] = {
+    make_variant<128, 4, 2, 3, true>("d128_tma_tt128_s3"),
+    make_variant<128, 4, 1, 6, true>("d128_tma_tt64_s6"),
+    make_variant<128, 4, 1, 3, true>("d128_tma_tt64_s3"),
+    make_variant<64, 4, 2, 6, true>("d64_tma_tt128_s6"),
+    make_variant<64, 4, 1, 6, true>("d64_tma_tt64_s6"),
+    make_variant<128, 4, 1, 1, false>("d128_generic_tt64"),
+    make_variant<64, 4, 1, 1, false>("d64_generic_tt64"),
+};
+constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
+constexpr int kDefaultTma128 = 0, kSmallTma128 = 1, kDefaultTma64 = 3, kSmallTma64 = 4;
+constexpr int kGeneric128 = 5, kGeneric64 = 6;
+
+// ------------------------------------------------------------ device cache
+struct DeviceState {
+  bool probed = false;
+  int sms = 0;
+  int major = 0;
+  int minor = 0;
+  bool prepared[kNumVariants] = {};
+  int blocks_per_sm[kNumVariants] = {};
+};
+constexpr int kMaxDevices = 64;
+std::mutex g_mutex;
+DeviceState g_devices[kMaxDevices];
+
+int forced_variant() {
+  static int forced = [] {
+    const char* name = std::getenv("ADB_KERNEL_VARIANT");
+    if (name == nullptr || *name == 0) return -1;
+    for (int i = 0; i < kNumVariants; ++i)
+      if (std::strcmp(name, kVariants[i].name) == 0) return i;
+    return -1;
+  }();
+  return forced;
+}
+
+int probe_device(int device, DeviceState** out) {
+  if (device < 0 || device >= kMaxDevices)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "device index %d out of range", device);
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceState& st = g_devices[device];
+  if (!st.probed) {
+    cudaError_t e = cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    e = cudaDeviceGetAttribute(&st.major, cudaDevAttrComputeCapabilityMajor, device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(major)");
+    e = cudaDeviceGetAttribute(&st.minor, cudaDevAttrComputeCapabilityMinor, device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(minor)");
+    st.probed = true;
+  }
+  if (st.major != 10)
+    return fail(ADB_ERR_DEVICE,
+                "this library requires an sm_100 GPU (compute capability 10.x); device %d is "
+                "%d.%d",
+                device, st.major, st.minor);
+  *out = &st;
+  return ADB_OK;
+}
+
+// Sets the dynamic shared-memory limit of a variant on the current device and
+// caches how many CTAs of it fit on one SM.
+int prepare_variant(DeviceState* st, int vi) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (st->prepared[vi]) return ADB_OK;
+  const Variant& v = kVariants[vi];
+  cudaError_t e =
+      cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem_bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+  int blocks = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, v.fn, v.threads, v.smem_bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  if (blocks < 1) return fail(ADB_ERR_CUDA, "kernel %s does not fit on an SM", v.name);
+  st->blocks_per_sm[vi] = blocks;
+  st->prepared[vi] = true;
+  return ADB_OK;
+}
+
+// ------------------------------------------------------------ TMA encode
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+cudaError_t g_encode_error = cudaSuccess;
+
+int get_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) {
+  std::call_once(g_encode_once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    g_encode_error =
+        cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q);
+    if (g_encode_error == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  if (g_encode == nullptr) {
+    if (g_encode_error != cudaSuccess) return cuda_fail(g_encode_error, "cuTensorMapEncodeTiled lookup");
+    return fail(ADB_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  }
+  *fn = g_encode;
+  return ADB_OK;
+}
+
+// 3-D map over one KV tensor viewed as [pairs][S][D] bf16; a box is
+// 64 columns (128 bytes, swizzled) x tile_tokens rows x 1 pair.  Rows past S
+// are outside the tensor and read as zeros.
+int encode_kv_map(CUtensorMap* map, const void* base, int64_t pairs, int64_t S, int64_t D,
+                  int tile_tokens) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  int rc = get_encoder(&encode);
+  if (rc != ADB_OK) return rc;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S),
+                        static_cast<cuuint64_t>(pairs)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(S * D * 2)};
+  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(tile_tokens), 1u};
+  cuuint32_t elem[3] = {1u, 1u, 1u};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                      strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ADB_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
+  return ADB_OK;
+}
+
+// ------------------------------------------------------------ plan
+struct Shape {
+  int64_t B, Hq, Hkv, S, D, G, P;
+};
+
+int check_shape(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t kv_len,
+                int64_t head_dim, Shape* s) {
+  if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || kv_len <= 0 || head_dim <= 0)
+    return fail(ADB_ERR_INVALID_ARGUMENT,
+                "all dimensions must be positive (empty tensors are unsupported): batch=%lld "
+                "q_heads=%lld kv_heads=%lld kv_len=%lld head_dim=%lld",
+                (long long)batch, (long long)q_heads, (long long)kv_heads, (long long)kv_len,
+                (long long)head_dim);
+  if (q_heads % kv_heads != 0)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "query heads (%lld) must be divisible by KV heads (%lld)",
+                (long long)q_heads, (long long)kv_heads);
+  const int64_t G = q_heads / kv_heads;
+  if (G != 1 && G != 4 && G != 8)
+    return fail(ADB_ERR_UNSUPPORTED, "supported GQA group sizes are 1, 4 and 8 (got %lld)",
+                (long long)G);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(ADB_ERR_UNSUPPORTED, "head dimension must be 64 or 128 (got %lld)",
+                (long long)head_dim);
+  if (kv_len > INT32_MAX)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "kv_len %lld exceeds 2^31-1", (long long)kv_len);
+  if (batch * kv_heads > INT32_MAX)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "batch*kv_heads exceeds 2^31-1");
+  *s = Shape{batch, q_heads, kv_heads, kv_len, head_dim, G, batch * kv_heads};
+  return ADB_OK;
+}
+
+struct Plan {
+  int variant;
+  int64_t num_ctas;
+  size_t off_acc, off_ml, off_cum, bytes;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+int choose_variant(const Shape& s, bool tma) {
+  if (!tma) return s.D == 128 ? kGeneric128 : kGeneric64;
+  const int forced = forced_variant();
+  if (forced >= 0 && kVariants[forced].head_dim == s.D && kVariants[forced].tma) return forced;
+  return s.D == 128 ? kDefaultTma128 : kDefaultTma64;
+}
+
+int make_plan(const Shape& s, bool varlen, bool tma, DeviceState* st, Plan* plan) {
+  int vi = choose_variant(s, tma);
+  // Small problems: prefer the 64-token tile so more SMs get work.
+  if (tma && forced_variant() < 0) {
+    const int64_t tiles = s.P * ((s.S + kVariants[vi].tile_tokens - 1) / kVariants[vi].tile_tokens);
+    if (tiles < 2LL * st->sms) vi = s.D == 128 ? kSmallTma128 : kSmallTma64;
+  }
+  int rc = prepare_variant(st, vi);
+  if (rc != ADB_OK) return rc;
+  const Variant& v = kVariants[vi];
+  const int64_t nt_max = s.P * ((s.S + v.tile_tokens - 1) / v.tile_tokens);
+  int64_t nc = static_cast<int64_t>(st->sms) * st->blocks_per_sm[vi];
+  if (nc > nt_max) nc = nt_max;
+  if (nc < 1) nc = 1;
+  plan->variant = vi;
+  plan->num_ctas = nc;
+  const size_t slots = static_cast<size_t>(nc + s.P);
+  plan->off_acc = 0;
+  plan->off_ml = align256(slots * s.G * s.D * sizeof(float));
+  plan->off_cum = plan->off_ml + align256(slots * s.G * 2 * sizeof(float));
+  plan->bytes = plan->off_cum + (varlen ? align256(static_cast<size_t>(s.B + 1) * 8) : 0);
+  return ADB_OK;
+}
+
+struct DeviceGuard {
+  int previous = -1;
+  bool switched = false;
+  cudaError_t error = cudaSuccess;
+  explicit DeviceGuard(int device) {
+    error = cudaGetDevice(&previous);
+    if (error == cudaSuccess && previous != device) {
+      error = cudaSetDevice(device);
+      switched = error == cudaSuccess;
+    }
+  }
+  ~DeviceGuard() {
+    if (switched) cudaSetDevice(previous);
+  }
+};
+
+bool is_aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// Whether any (pair) of a uniform-length problem straddles a CTA boundary.
+bool uniform_has_split(const Shape& s, int tile_tokens, int64_t nc) {
+  const int64_t nt = (s.S + tile_tokens - 1) / tile_tokens;
+  const int64_t total = s.P * nt;
+  for (int64_t c = 1; c < nc; ++c)
+    if ((c * total / nc) % nt != 0) return true;
+  return false;
+}
+
+int run_decode(const void* q, const void* k, const void* v, const int32_t* seqlens, void* out,
+               float* state_acc, float* state_ml, int64_t batch, int64_t q_heads, int64_t kv_heads,
+               int64_t kv_len, int64_t head_dim, void* workspace, size_t workspace_bytes,
+               int device, void* stream_ptr) {
+  Shape s;
+  int rc = check_shape(batch, q_heads, kv_heads, kv_len, head_dim, &s);
+  if (rc != ADB_OK) return rc;
+  const bool partial = state_acc != nullptr;
+  if (q == nullptr || k == nullptr || v == nullptr)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "Q, K and V pointers must be non-null");
+  if (!partial && out == nullptr) return fail(ADB_ERR_INVALID_ARGUMENT, "output pointer is null");
+  if (partial && state_ml == nullptr)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "partial-state pointers must be non-null");
+  DeviceGuard guard(device);
+  if (guard.error != cudaSuccess) return cuda_fail(guard.error, "cudaSetDevice");
+  DeviceState* st = nullptr;
+  rc = probe_device(device, &st);
+  if (rc != ADB_OK) return rc;
+  const bool tma = is_aligned(k, 16) && is_aligned(v, 16);
+  Plan plan;
+  rc = make_plan(s, seqlens != nullptr, tma, st, &plan);
+  if (rc != ADB_OK) return rc;
+  if (workspace == nullptr || !is_aligned(workspace, 256))
+    return fail(ADB_ERR_WORKSPACE, "workspace must be a non-null 256-byte aligned device buffer");
+  if (workspace_bytes < plan.bytes)
+    return fail(ADB_ERR_WORKSPACE, "workspace too small: %zu bytes given, %zu needed",
+                workspace_bytes, plan.bytes);
+  const Variant& var = kVariants[plan.variant];
+
+  CUtensorMap tm_k, tm_v;
+  std::memset(&tm_k, 0, sizeof(tm_k));
+  std::memset(&tm_v, 0, sizeof(tm_v));
+  if (var.tma) {
+    rc = encode_kv_map(&tm_k, k, s.P, s.S, s.D, var.tile_tokens);
+    if (rc != ADB_OK) return rc;
+    rc = encode_kv_map(&tm_v, v, s.P, s.S, s.D, var.tile_tokens);
+    if (rc != ADB_OK) return rc;
+  }
+
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  adb::DecodeParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.seqlens = seqlens;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.state_acc = state_acc;
+  p.state_ml = state_ml;
+  p.ws_acc = reinterpret_cast<float*>(ws + plan.off_acc);
+  p.ws_ml = reinterpret_cast<float*>(ws + plan.off_ml);
+  p.ws_cum = seqlens ? reinterpret_cast<int64_t*>(ws + plan.off_cum) : nullptr;
+  p.batch = s.B;
+  p.kv_heads = s.Hkv;
+  p.kv_len = s.S;
+  p.group = static_cast<int>(s.G);
+  p.partial_mode = partial ? 1 : 0;
+  p.num_ctas = static_cast<int>(plan.num_ctas);
+  p.tile_tokens = var.tile_tokens;
+  p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(s.D)));
+
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
+  if (t_timing.enabled) {
+    cudaError_t te = cudaEventCreate(&ev_start);
+    if (te == cudaSuccess) te = cudaEventCreate(&ev_stop);
+    if (te == cudaSuccess) te = cudaEventRecord(ev_start, stream);
+    if (te != cudaSuccess) return cuda_fail(te, "timing event");
+  }
+  void* args[] = {&tm_k, &tm_v, &p};
+  cudaError_t e = cudaLaunchKernel(var.fn, dim3(static_cast<unsigned>(plan.num_ctas)),
+                                   dim3(var.threads), args, var.smem_bytes, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (t_timing.enabled) {
+    e = cudaEventRecord(ev_stop, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "timing event");
+    t_timing.events.emplace_back(ev_start, ev_stop);
+  }
+
+  const bool need_combine =
+      seqlens != nullptr || uniform_has_split(s, var.tile_tokens, plan.num_ctas);
+  if (need_combine) {
+    const int64_t rows = s.P * s.G;
+    const int warps = 8;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((rows + warps - 1) / warps));
+    cfg.blockDim = dim3(warps * 32);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (s.D == 128)
+      e = cudaLaunchKernelEx(&cfg, adb::combine_segments_kernel<128>, p);
+    else
+      e = cudaLaunchKernelEx(&cfg, adb::combine_segments_kernel<64>, p);
+    if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+  }
+  return ADB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* adb_version(void) { return "attention_decode_b200 0.1.0 sm_100a"; }
+
+const char* adb_last_error(void) { return t_last_error.c_str(); }
+
+int adb_check_device(int device) {
+  DeviceState* st = nullptr;
+  return probe_device(device, &st);
+}
+
+int adb_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t kv_len,
+                              int64_t head_dim, int has_seqlens, int device, size_t* bytes) {
+  if (bytes == nullptr) return fail(ADB_ERR_INVALID_ARGUMENT, "bytes pointer is null");
+  Shape s;
+  int rc = check_shape(batch, q_heads, kv_heads, kv_len, head_dim, &s);
+  if (rc != ADB_OK) return rc;
+  DeviceGuard guard(device);
+  if (guard.error != cudaSuccess) return cuda_fail(guard.error, "cudaSetDevice");
+  DeviceState* st = nullptr;
+  rc = probe_device(device, &st);
+  if (rc != ADB_OK) return rc;
+  Plan a, b;
+  rc = make_plan(s, has_seqlens != 0, true, st, &a);
+  if (rc != ADB_OK) return rc;
+  rc = make_plan(s, has_seqlens != 0, false, st, &b);
+  if (rc != ADB_OK) return rc;
+  *bytes = a.bytes > b.bytes ? a.bytes : b.bytes;
+  return ADB_OK;
+}
+
+int adb_decode(const void* q, const void* k, const void* v, const int32_t* seqlens, void* out,
+               int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t kv_len, int64_t head_dim,
+               void* workspace, size_t workspace_bytes, int device, void* stream) {
+  return run_decode(q, k, v, seqlens, out, nullptr, nullptr, batch, q_heads, kv_heads, kv_len,
+                    head_dim, workspace, workspace_bytes, device, stream);
+}
+
+int adb_decode_partial(const void* q, const void* k, const void* v, const int32_t* seqlens,
+                       float* acc, float* ml, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                       int64_t kv_len, int64_t head_dim, void* workspace, size_t workspace_bytes,
+                       int device, void* stream) {
+  if (acc == nullptr || ml == nullptr)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "partial-state pointers must be non-null");
+  return run_decode(q, k, v, seqlens, nullptr, acc, ml, batch, q_heads, kv_heads, kv_len, head_dim,
+                    workspace, workspace_bytes, device, stream);
+}
+
+int adb_combine(const float* acc, int64_t acc_part_stride, const float* ml, int64_t ml_part_stride,
+                int64_t parts, int64_t rows, int64_t head_dim, void* out, int device, void* stream) {
+  if (acc == nullptr || ml == nullptr || out == nullptr)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "combine pointers must be non-null");
+  if (parts <= 0 || rows <= 0)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "parts and rows must be positive");
+  if (head_dim != 64 && head_dim != 128)
+    return fail(ADB_ERR_UNSUPPORTED, "head dimension must be 64 or 128 (got %lld)",
+                (long long)head_dim);
+  if (parts > 1 && (acc_part_stride < rows * head_dim || ml_part_stride < rows * 2))
+    return fail(ADB_ERR_INVALID_ARGUMENT,
+                "part strides (%lld, %lld) are smaller than one part (%lld, %lld floats)",
+                (long long)acc_part_stride, (long long)ml_part_stride, (long long)(rows * head_dim),
+                (long long)(rows * 2));
+  DeviceGuard guard(device);
+  if (guard.error != cudaSuccess) return cuda_fail(guard.error, "cudaSetDevice");
+  DeviceState* st = nullptr;
+  int rc = probe_device(device, &st);
+  if (rc != ADB_OK) return rc;
+  const int warps = 8;
+  const dim3 grid(static_cast<unsigned>((rows + warps - 1) / warps));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+  if (head_dim == 128)
+    adb::merge_states_kernel<128><<<grid, warps * 32, 0, s>>>(acc, acc_part_stride, ml,
+                                                            ml_part_stride, parts, rows, o);
+  else
+    adb::merge_states_kernel<64><<<grid, warps * 32, 0, s>>>(acc, acc_part_stride, ml,
+                                                           ml_part_stride, parts, rows, o);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return ADB_OK;
+}
+
+int adb_read_error_flag(int device, int* flag, int reset) {
+  if (flag == nullptr) return fail(ADB_ERR_INVALID_ARGUMENT, "flag pointer is null");
+  DeviceGuard guard(device);
+  if (guard.error != cudaSuccess) return cuda_fail(guard.error, "cudaSetDevice");
+  cudaError_t e = cudaMemcpyFromSymbol(flag, adb::g_adb_error_flag, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error flag");
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(adb::g_adb_error_flag, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "clearing the device error flag");
+  }
+  return ADB_OK;
+}
+
+int adb_launch_count(int64_t* launches) {
+  if (launches == nullptr) return fail(ADB_ERR_INVALID_ARGUMENT, "launches pointer is null");
+  *launches = g_launches.load(std::memory_order_relaxed);
+  return ADB_OK;
+}
+
+int adb_timing_enable(int enable) {
+  t_timing.enabled = enable != 0;
+  return ADB_OK;
+}
+
+int adb_timing_read(double* total_ms, int64_t* launches) {
+  if (total_ms == nullptr || launches == nullptr)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "output pointers must be non-null");
+  double sum = 0.0;
+  int64_t n = 0;
+  cudaError_t first_error = cudaSuccess;
+  for (auto& pr : t_timing.events) {
+    float ms = 0.f;
+    cudaError_t e = cudaEventSynchronize(pr.second);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, pr.first, pr.second);
+    if (e == cudaSuccess) {
+      sum += ms;
+      ++n;
+    } else if (first_error == cudaSuccess) {
+      first_error = e;
+    }
+    cudaEventDestroy(pr.first);
+    cudaEventDestroy(pr.second);
+  }
+  t_timing.events.clear();
+  *total_ms = sum;
+  *launches = n;
+  if (first_error != cudaSuccess) return cuda_fail(first_error, "reading timing events");
+  return ADB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,133 @@
+/*
+ * attention_decode_b200.h -- C ABI of the B200 (sm_100a) BF16 split-K
+ * attention-decode library (libattention_decode_b200.so).
+ *
+ * Operation (single query token per sequence, GQA):
+ *     O[b, hq, 0, :] = softmax(Q[b, hq, 0, :] . K[b, hq / G, :L_b, :]^T / sqrt(D))
+ *                      . V[b, hq / G, :L_b, :]
+ * with G = Hq / Hkv, every tensor BF16 and contiguous (BHSD layout), FP32
+ * softmax and accumulation.  L_b = S for every sequence unless a `seqlens`
+ * array is given.
+ *
+ * The library replaces the reference's CUDA extension entry point
+ *     at::Tensor attention_decode_cuda(q, k, v)      csrc/decode.cu:223-258
+ * bound to Python as `forward`                       csrc/binding.cpp:3-8
+ * with plain pointers, sizes and a caller-supplied stream and workspace, so
+ * any FFI (ctypes, cgo, JNI, N-API) can bind it.  No function allocates
+ * device memory, synchronises the host or keeps per-call state: every call is
+ * stream-ordered and may be captured in a CUDA graph, and concurrent calls on
+ * different streams are independent as long as their workspaces differ.
+ *
+ * Error convention: every function returns an adb_status; on failure a
+ * message is kept in thread-local storage (adb_last_error).  Argument errors
+ * are detected on the host before any launch, mirroring the TORCH_CHECKs at
+ * csrc/decode.cu:225-244.
+ */
+#ifndef ATTENTION_DECODE_B200_H
+#define ATTENTION_DECODE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ADB_API __attribute__((visibility("default")))
+#else
+#define ADB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum adb_status {
+  ADB_OK = 0,
+  ADB_ERR_INVALID_ARGUMENT = 1, /* sizes, null pointers, contract violations */
+  ADB_ERR_UNSUPPORTED = 2,      /* head_dim not in {64,128}, group not in {1,4,8} */
+  ADB_ERR_DEVICE = 3,           /* device is not compute capability 10.x      */
+  ADB_ERR_WORKSPACE = 4,        /* workspace missing, too small or misaligned  */
+  ADB_ERR_CUDA = 5              /* CUDA runtime error during set-up or launch  */
+} adb_status;
+
+/* Library version string, e.g. "attention_decode_b200 0.1.0 sm_100a". */
+ADB_API const char* adb_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+ADB_API const char* adb_last_error(void);
+
+/* Checks that `device` is a compute-capability 10.x GPU that this build can
+ * run on.  Replaces the per-call capability gate at csrc/decode.cu:243-244
+ * (which required 12.0). */
+ADB_API int adb_check_device(int device);
+
+/* Bytes of device workspace adb_decode / adb_decode_partial need for this
+ * problem on `device` (depends on the device's SM count).  `has_seqlens` is
+ * non-zero when a per-sequence length array will be passed.  Replaces the
+ * reference's internal `at::empty({heads, splits, D + 2})` partial buffer
+ * (csrc/decode.cu:205). */
+ADB_API int adb_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv_heads,
+                              int64_t kv_len, int64_t head_dim, int has_seqlens,
+                              int device, size_t* bytes);
+
+/* Full decode into a BF16 output [batch, q_heads, 1, head_dim].
+ *   q        [batch, q_heads, 1, head_dim]       bf16, contiguous
+ *   k, v     [batch, kv_heads, kv_len, head_dim] bf16, contiguous
+ *   seqlens  NULL, or int32 [batch] on the device: sequence b uses its first
+ *            seqlens[b] tokens (values are clamped to [0, kv_len]; a length
+ *            of 0 gives an all-zero output row, as the FP32 oracle does)
+ *   out      [batch, q_heads, 1, head_dim]       bf16
+ *   workspace at least adb_decode_workspace_size() bytes, 256-byte aligned
+ *   stream   cudaStream_t (NULL = legacy default stream)
+ * Replaces attention_decode_cuda (csrc/decode.cu:223-258) and its launch path
+ * decode_bf16_mma + merge_splits (csrc/decode.cu:70-211).  K/V pointers that
+ * are not 16-byte aligned are accepted (slower fallback path), matching the
+ * reference's unaligned dispatch (csrc/decode.cu:212-220). */
+ADB_API int adb_decode(const void* q, const void* k, const void* v, const int32_t* seqlens,
+               void* out, int64_t batch, int64_t q_heads, int64_t kv_heads,
+               int64_t kv_len, int64_t head_dim, void* workspace,
+               size_t workspace_bytes, int device, void* stream);
+
+/* Partial decode for sequence sharding: instead of the normalised output it
+ * writes, per query-head row r = b * q_heads + hq,
+ *   acc[r, 0:head_dim]  unnormalised sum_t exp(s_t - m) * V_t   (fp32)
+ *   ml[r, 0] = m        max logit s_t = q.k_t / sqrt(D) (natural units)
+ *   ml[r, 1] = l        sum_t exp(s_t - m)
+ * over this call's KV.  An empty sequence gives acc = 0, m = -inf, l = 0.
+ * The state layout is the reference's split partial (acc[D], m, l)
+ * (csrc/decode.cu:127-129,160), kept as two arrays. */
+ADB_API int adb_decode_partial(const void* q, const void* k, const void* v,
+                       const int32_t* seqlens, float* acc, float* ml,
+                       int64_t batch, int64_t q_heads, int64_t kv_heads,
+                       int64_t kv_len, int64_t head_dim, void* workspace,
+                       size_t workspace_bytes, int device, void* stream);
+
+/* Merges `parts` partial states per row into BF16 output rows:
+ *   M = max_r m_r,  O = sum_r e^(m_r - M) acc_r / sum_r e^(m_r - M) l_r.
+ * Part r's arrays start at acc + r * acc_part_stride and
+ * ml + r * ml_part_stride (floats; rows are contiguous inside a part), so an
+ * all-gathered buffer of packed [acc | ml] blocks can be merged in place.
+ * Rows whose every part is empty (l = 0) become zeros.
+ * Replaces merge_splits (csrc/decode.cu:169-184) for the cross-GPU merge. */
+ADB_API int adb_combine(const float* acc, int64_t acc_part_stride, const float* ml,
+                        int64_t ml_part_stride, int64_t parts, int64_t rows,
+                        int64_t head_dim, void* out, int device, void* stream);
+
+/* Reads (and optionally clears) the sticky device error word that kernels
+ * set when a bounded wait gives up; 0 means no kernel has reported an
+ * error on `device`.  Synchronous (a device-to-host copy); for diagnostics. */
+ADB_API int adb_read_error_flag(int device, int* flag, int reset);
+
+/* Diagnostics (no reference counterpart: the reference has no instrumentation).
+ * adb_launch_count: kernels this process has launched through the library.
+ * adb_timing_enable: on the calling thread, record a CUDA event pair around
+ *   every partial (streaming) kernel launched from then on.
+ * adb_timing_read: wait for the recorded events, return the summed duration
+ *   in milliseconds and the number of timed launches, and forget them. */
+ADB_API int adb_launch_count(int64_t* launches);
+ADB_API int adb_timing_enable(int enable);
+ADB_API int adb_timing_read(double* total_ms, int64_t* launches);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ATTENTION_DECODE_B200_H */

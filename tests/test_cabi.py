@@ -1,0 +1,98 @@
+"""The C-ABI library loads, exports every function include/*.h declares, and
+rejects bad arguments on the host.  CPU only: no call here reaches a device."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from attention_decode import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+
+
+def declared_functions():
+    names = []
+    for header in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+        names += re.findall(r"ADB_API\s+[\w\s\*]+?\b(adb_\w+)\s*\(", text)
+    return sorted(set(names))
+
+
+def test_headers_declare_the_entry_points():
+    names = declared_functions()
+    for expected in ("adb_decode", "adb_decode_partial", "adb_combine", "adb_decode_workspace_size"):
+        assert expected in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load_library()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+        assert name in _lib.PROTOTYPES, f"{name} has no ctypes prototype"
+
+
+def test_version_and_empty_last_error():
+    lib = _lib.load_library()
+    assert b"sm_100a" in lib.adb_version()
+    assert isinstance(lib.adb_last_error(), bytes)
+
+
+@pytest.mark.parametrize(
+    "shape,status,pattern",
+    [
+        ((0, 32, 8, 129, 64), _lib.ADB_ERR_INVALID_ARGUMENT, "positive"),
+        ((1, 32, 0, 129, 64), _lib.ADB_ERR_INVALID_ARGUMENT, "positive"),
+        ((1, 32, 8, 0, 64), _lib.ADB_ERR_INVALID_ARGUMENT, "positive"),
+        ((1, 31, 8, 129, 64), _lib.ADB_ERR_INVALID_ARGUMENT, "divisible"),
+        ((1, 32, 16, 129, 64), _lib.ADB_ERR_UNSUPPORTED, "group"),
+        ((1, 32, 4, 129, 64) , _lib.ADB_OK, None),
+        ((1, 32, 8, 129, 96), _lib.ADB_ERR_UNSUPPORTED, "head dimension"),
+        ((1, 32, 8, 129, 32), _lib.ADB_ERR_UNSUPPORTED, "head dimension"),
+        ((1, 32, 8, 2**31, 64), _lib.ADB_ERR_INVALID_ARGUMENT, "kv_len"),
+    ],
+)
+def test_workspace_query_validates_shapes_on_host(shape, status, pattern):
+    if status == _lib.ADB_OK:
+        pytest.skip("valid shape: the query would touch the device")
+    lib = _lib.load_library()
+    out = ctypes.c_size_t(0)
+    rc = lib.adb_decode_workspace_size(*shape, 0, 0, ctypes.byref(out))
+    assert rc == status
+    assert re.search(pattern, _lib.last_error(lib))
+
+
+def test_null_pointers_are_rejected_before_launch():
+    lib = _lib.load_library()
+    rc = lib.adb_decode(None, None, None, None, None, 1, 32, 8, 129, 64, None, 0, 0, None)
+    assert rc == _lib.ADB_ERR_INVALID_ARGUMENT
+    assert "non-null" in _lib.last_error(lib)
+    rc = lib.adb_combine(None, 0, None, 0, 1, 1, 64, None, 0, None)
+    assert rc == _lib.ADB_ERR_INVALID_ARGUMENT
+
+
+def test_check_raises_typed_error():
+    lib = _lib.load_library()
+    lib.adb_combine(None, 0, None, 0, 1, 1, 64, None, 0, None)
+    with pytest.raises(_lib.AttentionDecodeError) as info:
+        _lib.check(lib, _lib.ADB_ERR_INVALID_ARGUMENT)
+    assert isinstance(info.value, RuntimeError)
+    assert info.value.status == _lib.ADB_ERR_INVALID_ARGUMENT
+
+
+def test_python_api_rejects_cpu_inputs():
+    """tests/test_attention_decode.py:242-251."""
+    import torch
+
+    from attention_decode import attention_decode
+
+    q = torch.randn(1, 32, 1, 64, dtype=torch.bfloat16)
+    k = torch.randn(1, 8, 129, 64, dtype=torch.bfloat16)
+    with pytest.raises((ValueError, RuntimeError, TypeError), match="(?i)cuda|device"):
+        attention_decode(q, k, k)
+    with pytest.raises(TypeError):
+        attention_decode(None, k, k)
