@@ -92,22 +92,63 @@ def _validate(q, k, v, seqlens=None):
             _fail("seqlens must be a contiguous [batch] tensor")
 
 
-def workspace_bytes(batch, q_heads, kv_heads, kv_len, head_dim, has_seqlens=False, device=0) -> int:
-    """Device workspace one decode call needs (adb_decode_workspace_size)."""
+def workspace_bytes(batch, q_heads, kv_heads, kv_len, head_dim, has_seqlens=False, device=0) -> tuple[int, int]:
+    """(workspace bytes, scheduler-header bytes) one decode call needs
+    (adb_decode_workspace_size)."""
     key = (batch, q_heads, kv_heads, kv_len, head_dim, bool(has_seqlens), device)
     cached = _ws_cache.get(key)
     if cached is not None:
         return cached
     lib = _lib.load_library()
-    out = ctypes.c_size_t(0)
+    total, header = ctypes.c_size_t(0), ctypes.c_size_t(0)
     _lib.check(
         lib,
         lib.adb_decode_workspace_size(
-            batch, q_heads, kv_heads, kv_len, head_dim, int(bool(has_seqlens)), device, ctypes.byref(out)
+            batch, q_heads, kv_heads, kv_len, head_dim, int(bool(has_seqlens)), device,
+            ctypes.byref(total), ctypes.byref(header),
         ),
     )
-    _ws_cache[key] = out.value
-    return out.value
+    _ws_cache[key] = (total.value, header.value)
+    return _ws_cache[key]
+
+
+# One workspace per (device, stream): calls on one stream are ordered, and each
+# completed call leaves its scheduler header (the first `header` bytes) zero
+# again, so no per-call memset is needed while the header fits in the prefix
+# known to be zero.  A call whose header is larger than that prefix (another
+# problem shape wrote segment data there) lets the library zero it.
+# Concurrent streams get separate workspaces.  (The reference allocates its
+# partial buffer per call from the caching allocator, csrc/decode.cu:205.)
+_stream_workspaces: dict = {}
+_MAX_STREAM_WORKSPACES = 64
+
+
+class _StreamWorkspace:
+    __slots__ = ("buf", "clean")
+
+    def __init__(self, buf):
+        self.buf = buf
+        self.clean = buf.numel()  # bytes known to be zero
+
+
+def _workspace(device_obj, device: int, stream: int, nbytes: int, header: int):
+    torch = _torch()
+    nbytes = max(nbytes, 256)
+    if torch.cuda.is_current_stream_capturing():
+        # A captured call owns its buffer in the graph's pool; the library's
+        # header memset is captured with it.
+        return torch.empty(nbytes, dtype=torch.uint8, device=device_obj), 0
+    key = (device, stream)
+    ws = _stream_workspaces.get(key)
+    if ws is None or ws.buf.numel() < nbytes:
+        if ws is None and len(_stream_workspaces) >= _MAX_STREAM_WORKSPACES:
+            # Buffers are freed stream-ordered on the stream that used them.
+            _stream_workspaces.pop(next(iter(_stream_workspaces)))
+        ws = _StreamWorkspace(torch.zeros(nbytes, dtype=torch.uint8, device=device_obj))
+        _stream_workspaces[key] = ws
+    flags = _lib.ADB_FLAG_HEADER_ZEROED if header <= ws.clean else 0
+    ws.clean = header  # after the call only its own header is guaranteed zero
+    return ws.buf, flags
 
 
 def _launch(q, k, v, seqlens, out=None, acc=None, ml=None):
@@ -116,23 +157,21 @@ def _launch(q, k, v, seqlens, out=None, acc=None, ml=None):
     batch, q_heads, _, head_dim = q.shape
     kv_heads, kv_len = k.shape[1], k.shape[2]
     device = q.device.index if q.device.index is not None else torch.cuda.current_device()
-    nbytes = workspace_bytes(batch, q_heads, kv_heads, kv_len, head_dim, seqlens is not None, device)
-    # Stream-ordered scratch from the caching allocator: safe under CUDA graphs
-    # and concurrent streams (reference: at::empty partial, csrc/decode.cu:205).
-    workspace = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=q.device)
+    nbytes, header = workspace_bytes(batch, q_heads, kv_heads, kv_len, head_dim, seqlens is not None, device)
     stream = torch.cuda.current_stream(q.device).cuda_stream
+    workspace, flags = _workspace(q.device, device, stream, nbytes, header)
     lens = seqlens.data_ptr() if seqlens is not None else None
     if out is not None:
         status = lib.adb_decode(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), lens, out.data_ptr(),
             batch, q_heads, kv_heads, kv_len, head_dim,
-            workspace.data_ptr(), workspace.numel(), device, stream,
+            workspace.data_ptr(), workspace.numel(), flags, device, stream,
         )
     else:
         status = lib.adb_decode_partial(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), lens, acc.data_ptr(), ml.data_ptr(),
             batch, q_heads, kv_heads, kv_len, head_dim,
-            workspace.data_ptr(), workspace.numel(), device, stream,
+            workspace.data_ptr(), workspace.numel(), flags, device, stream,
         )
     _lib.check(lib, status)
 

@@ -24,6 +24,7 @@ ADB_ERR_UNSUPPORTED = 2
 ADB_ERR_DEVICE = 3
 ADB_ERR_WORKSPACE = 4
 ADB_ERR_CUDA = 5
+ADB_FLAG_HEADER_ZEROED = 1
 
 STATUS_NAMES = {
     ADB_OK: "ok",
@@ -39,21 +40,22 @@ _i64 = ctypes.c_int64
 _vp = ctypes.c_void_p
 _int = ctypes.c_int
 _size = ctypes.c_size_t
+_uint = ctypes.c_uint
 PROTOTYPES = {
     "adb_version": (ctypes.c_char_p, []),
     "adb_last_error": (ctypes.c_char_p, []),
     "adb_check_device": (_int, [_int]),
     "adb_decode_workspace_size": (
         _int,
-        [_i64, _i64, _i64, _i64, _i64, _int, _int, ctypes.POINTER(_size)],
+        [_i64, _i64, _i64, _i64, _i64, _int, _int, ctypes.POINTER(_size), ctypes.POINTER(_size)],
     ),
     "adb_decode": (
         _int,
-        [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _size, _int, _vp],
+        [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _size, _uint, _int, _vp],
     ),
     "adb_decode_partial": (
         _int,
-        [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _size, _int, _vp],
+        [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _size, _uint, _int, _vp],
     ),
     "adb_combine": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
     "adb_read_error_flag": (_int, [_int, ctypes.POINTER(_int), _int]),

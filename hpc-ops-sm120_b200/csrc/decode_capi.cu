@@ -105,6 +105,24 @@ int forced_variant() {
   return forced;
 }
 
+// ADB_DETERMINISTIC=1 turns off dynamic load balancing: every CTA processes
+// exactly its static range, so repeated calls give bit-identical results.
+// Tuning knobs read once from the environment (for measurement sweeps):
+// ADB_MAX_STEALS (default by problem size) and ADB_CLAIM_DIVISOR (default 4).
+int env_int(const char* name, int fallback) {
+  const char* v = std::getenv(name);
+  if (v == nullptr || *v == 0) return fallback;
+  return std::atoi(v);
+}
+
+bool deterministic_mode() {
+  static bool on = [] {
+    const char* v = std::getenv("ADB_DETERMINISTIC");
+    return v != nullptr && *v != 0 && std::strcmp(v, "0") != 0;
+  }();
+  return on;
+}
+
 int probe_device(int device, DeviceState** out) {
   if (device < 0 || device >= kMaxDevices)
     return fail(ADB_ERR_INVALID_ARGUMENT, "device index %d out of range", device);
@@ -219,10 +237,16 @@ int check_shape(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t kv_len
   return ADB_OK;
 }
 
+// Workspace layout (offsets 256-byte aligned):
+//   header, zero on entry and left zero by every completed call:
+//     claims u64[Nc] | counters u32[2] | done u64[P] (8-aligned) | slot_pair u32[dyn]
+//   acc f32[(Nc+P+dyn)*G*D] | ml f32[(Nc+P+dyn)*G*2]
 struct Plan {
   int variant;
   int64_t num_ctas;
-  size_t off_acc, off_ml, off_cum, bytes;
+  int64_t dyn_slots;
+  size_t off_claims, off_counters, off_done, off_slot_pair, header_bytes;
+  size_t off_acc, off_ml, bytes;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -250,11 +274,16 @@ int make_plan(const Shape& s, bool varlen, bool tma, DeviceState* st, Plan* plan
   if (nc < 1) nc = 1;
   plan->variant = vi;
   plan->num_ctas = nc;
-  const size_t slots = static_cast<size_t>(nc + s.P);
-  plan->off_acc = 0;
-  plan->off_ml = align256(slots * s.G * s.D * sizeof(float));
-  plan->off_cum = plan->off_ml + align256(slots * s.G * 2 * sizeof(float));
-  plan->bytes = plan->off_cum + (varlen ? align256(static_cast<size_t>(s.B + 1) * 8) : 0);
+  plan->dyn_slots = v.tma ? adb::dynamic_slot_capacity(nc) : 0;
+  const size_t slots = static_cast<size_t>(nc + s.P + plan->dyn_slots);
+  plan->off_claims = 0;
+  plan->off_counters = static_cast<size_t>(nc) * 8;
+  plan->off_done = plan->off_counters + 8;
+  plan->off_slot_pair = plan->off_done + static_cast<size_t>(s.P) * 8;
+  plan->header_bytes = plan->off_slot_pair + static_cast<size_t>(plan->dyn_slots) * 4;
+  plan->off_acc = align256(plan->header_bytes);
+  plan->off_ml = plan->off_acc + align256(slots * s.G * s.D * sizeof(float));
+  plan->bytes = plan->off_ml + align256(slots * s.G * 2 * sizeof(float));
   return ADB_OK;
 }
 
@@ -276,19 +305,10 @@ struct DeviceGuard {
 
 bool is_aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
-// Whether any (pair) of a uniform-length problem straddles a CTA boundary.
-bool uniform_has_split(const Shape& s, int tile_tokens, int64_t nc) {
-  const int64_t nt = (s.S + tile_tokens - 1) / tile_tokens;
-  const int64_t total = s.P * nt;
-  for (int64_t c = 1; c < nc; ++c)
-    if ((c * total / nc) % nt != 0) return true;
-  return false;
-}
-
 int run_decode(const void* q, const void* k, const void* v, const int32_t* seqlens, void* out,
                float* state_acc, float* state_ml, int64_t batch, int64_t q_heads, int64_t kv_heads,
                int64_t kv_len, int64_t head_dim, void* workspace, size_t workspace_bytes,
-               int device, void* stream_ptr) {
+               unsigned flags, int device, void* stream_ptr) {
   Shape s;
   int rc = check_shape(batch, q_heads, kv_heads, kv_len, head_dim, &s);
   if (rc != ADB_OK) return rc;
@@ -335,17 +355,33 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
   p.state_ml = state_ml;
   p.ws_acc = reinterpret_cast<float*>(ws + plan.off_acc);
   p.ws_ml = reinterpret_cast<float*>(ws + plan.off_ml);
-  p.ws_cum = seqlens ? reinterpret_cast<int64_t*>(ws + plan.off_cum) : nullptr;
+  p.ws_claims = reinterpret_cast<unsigned long long*>(ws + plan.off_claims);
+  p.ws_counters = reinterpret_cast<uint32_t*>(ws + plan.off_counters);
+  p.ws_done = reinterpret_cast<unsigned long long*>(ws + plan.off_done);
+  p.ws_slot_pair = reinterpret_cast<uint32_t*>(ws + plan.off_slot_pair);
   p.batch = s.B;
   p.kv_heads = s.Hkv;
   p.kv_len = s.S;
   p.group = static_cast<int>(s.G);
   p.partial_mode = partial ? 1 : 0;
-  p.num_ctas = static_cast<int>(plan.num_ctas);
-  p.tile_tokens = var.tile_tokens;
+  // Stealing pays for itself when each CTA streams long enough for the SMs'
+  // unequal HBM shares to spread their finish times by more than the cost of
+  // the extra segments it creates (about 192 tiles per CTA).
+  static const int forced_steals = env_int("ADB_MAX_STEALS", -1);
+  static const int claim_divisor = env_int("ADB_CLAIM_DIVISOR", 4);
+  const int64_t tiles_per_cta =
+      s.P * ((s.S + var.tile_tokens - 1) / var.tile_tokens) / plan.num_ctas;
+  p.max_steals = forced_steals >= 0 ? forced_steals : (tiles_per_cta >= 192 ? adb::kMaxSteals : 0);
+  p.claim_divisor = claim_divisor >= 2 ? claim_divisor : 2;
+  p.steal = (var.tma && !deterministic_mode() && p.max_steals > 0) ? 1 : 0;
+  p.dyn_capacity = plan.dyn_slots;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(s.D)));
 
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (!(flags & ADB_FLAG_HEADER_ZEROED)) {
+    cudaError_t me = cudaMemsetAsync(ws, 0, plan.header_bytes, stream);
+    if (me != cudaSuccess) return cuda_fail(me, "workspace header memset");
+  }
   cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
   if (t_timing.enabled) {
     cudaError_t te = cudaEventCreate(&ev_start);
@@ -353,38 +389,27 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
     if (te == cudaSuccess) te = cudaEventRecord(ev_start, stream);
     if (te != cudaSuccess) return cuda_fail(te, "timing event");
   }
+  // Programmatic stream serialisation: the kernel may launch while the
+  // previous kernel in the stream drains; it waits (griddepcontrol.wait)
+  // before touching global memory.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(plan.num_ctas));
+  cfg.blockDim = dim3(var.threads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(var.smem_bytes);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   void* args[] = {&tm_k, &tm_v, &p};
-  cudaError_t e = cudaLaunchKernel(var.fn, dim3(static_cast<unsigned>(plan.num_ctas)),
-                                   dim3(var.threads), args, var.smem_bytes, stream);
+  cudaError_t e = cudaLaunchKernelExC(&cfg, var.fn, args);
   if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   if (t_timing.enabled) {
     e = cudaEventRecord(ev_stop, stream);
     if (e != cudaSuccess) return cuda_fail(e, "timing event");
     t_timing.events.emplace_back(ev_start, ev_stop);
-  }
-
-  const bool need_combine =
-      seqlens != nullptr || uniform_has_split(s, var.tile_tokens, plan.num_ctas);
-  if (need_combine) {
-    const int64_t rows = s.P * s.G;
-    const int warps = 8;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>((rows + warps - 1) / warps));
-    cfg.blockDim = dim3(warps * 32);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (s.D == 128)
-      e = cudaLaunchKernelEx(&cfg, adb::combine_segments_kernel<128>, p);
-    else
-      e = cudaLaunchKernelEx(&cfg, adb::combine_segments_kernel<64>, p);
-    if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
-    g_launches.fetch_add(1, std::memory_order_relaxed);
   }
   return ADB_OK;
 }
@@ -403,7 +428,8 @@ int adb_check_device(int device) {
 }
 
 int adb_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t kv_len,
-                              int64_t head_dim, int has_seqlens, int device, size_t* bytes) {
+                              int64_t head_dim, int has_seqlens, int device, size_t* bytes,
+                              size_t* header_bytes) {
   if (bytes == nullptr) return fail(ADB_ERR_INVALID_ARGUMENT, "bytes pointer is null");
   Shape s;
   int rc = check_shape(batch, q_heads, kv_heads, kv_len, head_dim, &s);
@@ -419,24 +445,25 @@ int adb_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv_heads, 
   rc = make_plan(s, has_seqlens != 0, false, st, &b);
   if (rc != ADB_OK) return rc;
   *bytes = a.bytes > b.bytes ? a.bytes : b.bytes;
+  if (header_bytes != nullptr) *header_bytes = a.header_bytes > b.header_bytes ? a.header_bytes : b.header_bytes;
   return ADB_OK;
 }
 
 int adb_decode(const void* q, const void* k, const void* v, const int32_t* seqlens, void* out,
                int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t kv_len, int64_t head_dim,
-               void* workspace, size_t workspace_bytes, int device, void* stream) {
+               void* workspace, size_t workspace_bytes, unsigned flags, int device, void* stream) {
   return run_decode(q, k, v, seqlens, out, nullptr, nullptr, batch, q_heads, kv_heads, kv_len,
-                    head_dim, workspace, workspace_bytes, device, stream);
+                    head_dim, workspace, workspace_bytes, flags, device, stream);
 }
 
 int adb_decode_partial(const void* q, const void* k, const void* v, const int32_t* seqlens,
                        float* acc, float* ml, int64_t batch, int64_t q_heads, int64_t kv_heads,
                        int64_t kv_len, int64_t head_dim, void* workspace, size_t workspace_bytes,
-                       int device, void* stream) {
+                       unsigned flags, int device, void* stream) {
   if (acc == nullptr || ml == nullptr)
     return fail(ADB_ERR_INVALID_ARGUMENT, "partial-state pointers must be non-null");
   return run_decode(q, k, v, seqlens, nullptr, acc, ml, batch, q_heads, kv_heads, kv_len, head_dim,
-                    workspace, workspace_bytes, device, stream);
+                    workspace, workspace_bytes, flags, device, stream);
 }
 
 int adb_combine(const float* acc, int64_t acc_part_stride, const float* ml, int64_t ml_part_stride,

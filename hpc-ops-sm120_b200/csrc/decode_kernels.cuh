@@ -1,25 +1,48 @@
 // decode_kernels.cuh -- BF16 split-K attention-decode kernels for sm_100a.
 //
-// Work decomposition (replaces the reference's fixed 256-token split grid,
-// csrc/decode.cu:193-211):
+// One decode call is ONE kernel launch (replaces the reference's partial
+// kernel + merge kernel pair and its fixed 256-token split grid,
+// csrc/decode.cu:193-211).
+//
+// Work decomposition:
 //   * A "pair" is one (batch, kv_head); its KV rows are contiguous in HBM at
 //     row offset pair * S of the [B*Hkv*S, D] view.  Pair p has L_p valid
 //     tokens (S, or seqlens[b]) cut into nt_p = ceil(L_p / TT) tiles of TT
 //     tokens.  All tiles of all pairs form one flattened tile space of NT
-//     tiles, and persistent CTA c of Nc streams the contiguous range
-//     [c*NT/Nc, (c+1)*NT/Nc).  Every CTA therefore moves the same number of
-//     bytes (+-1 tile) whatever B, Hkv and S are.
-//   * The part of a pair covered by one CTA is a "segment".  A segment that
-//     covers its whole pair is normalised and written as BF16 directly; any
-//     other segment writes an FP32 state (acc[G][D], m, l) into workspace
-//     slot (c + p) -- unique because both c and p are non-decreasing along
-//     the flattened space -- and the combine kernel merges the slots
-//     first_cta(p)+p .. last_cta(p)+p of each split pair.
+//     tiles, and persistent CTA c of Nc owns the contiguous range
+//     [c*NT/Nc, (c+1)*NT/Nc).
+//   * Load balancing: SMs do not stream HBM at equal rates (their finish
+//     times spread by ~20% under a static split), so a CTA whose range is
+//     exhausted becomes a thief and takes unclaimed tiles from the CTA with
+//     the most left.  Softmax state does not depend on tile order, so an
+//     owner folds every tile of a pair it processed into one state whatever
+//     was stolen in between.
+//   * The part of a pair one CTA processed is a "segment".  An owner that
+//     processed all of a pair's tiles writes the normalised BF16 output (or,
+//     in partial mode, the state) directly.  Any other segment is written to
+//     a workspace slot -- owners to slot (c + p), which is unique because c
+//     and p are both non-decreasing along the flattened space (an owner whose
+//     tiles of p were all stolen writes an empty state there), thieves to a
+//     dynamically allocated slot tagged with its pair -- and then committed
+//     by adding (owner ? 2^48 : 2^32) + tiles to the pair's counter.  The
+//     committer that brings the owner and tile fields to (owners(p), nt_p)
+//     merges all segments of p and writes the output: the split-K reduction
+//     happens inside the same kernel, by whichever CTA finishes the pair last.
+//   * Processing order: a CTA first processes its part of the pair it shares
+//     with the next CTA, so the merges of pairs split between owners happen
+//     early and overlap the stream; the last 1/claim_divisor of its range is
+//     claimable, one tile at a time by the owner and in chunks of up to
+//     kStealChunk tiles (from the back) by thieves.
+//   * Scheduler state (claim counters, pair counters, slot tags) lives in a
+//     workspace header that must be zero on entry; the last CTA to finish
+//     resets it, so a workspace reused by stream-ordered calls is zeroed
+//     once.
 //
-// Partial kernel (replaces decode_bf16_mma, csrc/decode.cu:70-167):
+// Streaming (replaces decode_bf16_mma, csrc/decode.cu:70-167):
 //   * one producer warp issues 3-D TMA tiled loads (cp.async.bulk.tensor,
 //     128-byte swizzle, no multicast) of the K and V tiles into a kStages
-//     deep shared-memory ring with full/empty mbarriers;
+//     deep shared-memory ring with full/empty mbarriers; a 32-byte record per
+//     stage tells the consumers which tile it holds;
 //   * kWarps consumer warps each own 16*kMB tokens of every tile and keep an
 //     independent online-softmax state; Q.K^T and P.V run on the tensor
 //     cores as m16n8k16 BF16 MMAs with the tokens as M and the GQA query
@@ -37,6 +60,16 @@ namespace adb {
 
 constexpr int kMaxGroup = 8;
 constexpr float kLn2 = 0.693147180559945309f;
+constexpr int kMaxSteals = 16;          // most steals one thief CTA may make (sizes the workspace)
+constexpr int kMaxTableBatches = 1024;  // varlen: per-batch tile table kept in shared memory
+constexpr int kStealChunk = 4;          // most tiles one steal takes
+constexpr int kStealMinRemaining = 4;   // a victim with fewer claimable tiles is left alone
+
+// Dynamic (thief) segment slots a launch of `nc` CTAs can create: each steal
+// takes at most kStealChunk tiles, so it adds at most that many segments.
+__host__ __device__ constexpr int64_t dynamic_slot_capacity(int64_t nc) {
+  return nc * (kStealChunk * kMaxSteals + 2);
+}
 
 struct DecodeParams {
   const __nv_bfloat16* q;  // [B*Hq, D]
@@ -46,16 +79,25 @@ struct DecodeParams {
   __nv_bfloat16* out;      // final mode: [B*Hq, D]
   float* state_acc;        // partial mode: [B*Hq, D]
   float* state_ml;         // partial mode: [B*Hq, 2]  (m natural units, l)
-  float* ws_acc;           // [(Nc + P) * G, D]
-  float* ws_ml;            // [(Nc + P) * G, 2]        (m log2 units, l)
-  int64_t* ws_cum;         // varlen: [B + 1] exclusive tile prefix per batch, [B] = NT
+  float* ws_acc;           // [(Nc + P + dyn) * G, D]   segment accumulators
+  float* ws_ml;            // [(Nc + P + dyn) * G, 2]   (m log2 units, l)
+  // workspace header: zero on entry and on exit
+  // [Nc] claims on each CTA's claimable positions: owner count from the
+  // front in the low 32 bits, thief count from the back in the high 32 bits
+  unsigned long long* ws_claims;
+  uint32_t* ws_counters;           // [0] dynamic slots handed out, [1] CTAs finished
+  // [P] per pair: (owner segments << 48) + (thief segments << 32) + tiles
+  unsigned long long* ws_done;
+  uint32_t* ws_slot_pair;          // [dyn] pair + 1 of each dynamic (thief) slot
   int64_t batch;
   int64_t kv_heads;
   int64_t kv_len;
   int group;
   int partial_mode;
-  int num_ctas;
-  int tile_tokens;
+  int steal;         // 1: dynamic load balancing enabled
+  int max_steals;    // steals per thief CTA (<= kMaxSteals)
+  int claim_divisor; // the last 1/claim_divisor of each range is claimable
+  int64_t dyn_capacity;  // dynamic slots the workspace holds
   float scale_log2;  // log2(e) / sqrt(D)
 };
 
@@ -67,6 +109,10 @@ __device__ __forceinline__ int32_t clamped_len(const DecodeParams& p, int64_t b)
   if (len < 0) len = 0;
   if (len > p.kv_len) len = static_cast<int32_t>(p.kv_len);
   return len;
+}
+
+__device__ __forceinline__ int64_t tiles_of(int32_t len, int tt) {
+  return (static_cast<int64_t>(len) + tt - 1) / tt;
 }
 
 // CTA whose tile range [c*NT/Nc, (c+1)*NT/Nc) contains tile t.
@@ -87,7 +133,7 @@ __device__ __forceinline__ void walk_set_batch(Walk& w, const DecodeParams& p, i
                                                int tt) {
   w.b = b;
   w.len = clamped_len(p, b);
-  w.nt = (static_cast<int64_t>(w.len) + tt - 1) / tt;
+  w.nt = tiles_of(w.len, tt);
 }
 
 __device__ __forceinline__ void walk_next(Walk& w, const DecodeParams& p, int tt) {
@@ -101,6 +147,15 @@ __device__ __forceinline__ void walk_next(Walk& w, const DecodeParams& p, int tt
   }
   w.b = p.batch;  // past the end; never dereferenced
   w.nt = 0;
+}
+
+// Tile t of batch b whose tiles start at flattened index `base`.
+__device__ __forceinline__ void walk_locate(Walk& w, const DecodeParams& p, int64_t b,
+                                            int64_t base, int64_t t, int tt) {
+  walk_set_batch(w, p, b, tt);
+  const int64_t r = t - base;
+  w.h = r / w.nt;
+  w.tile = r - w.h * w.nt;
 }
 
 // Inclusive block-wide scan of one int64 per thread.  `scratch` holds >= 33
@@ -132,6 +187,36 @@ __device__ __forceinline__ int64_t block_inclusive_scan(int64_t x, int64_t* scra
   return x + prefix;
 }
 
+enum : int32_t { kMetaOwn = 0, kMetaStolen = 1, kMetaEndOwn = 2, kMetaEndAll = 3 };
+
+// What one ring stage holds (written by the producer before the stage's
+// full-barrier arrive, read by the consumers after their wait).
+struct TileMeta {
+  int64_t tile;  // flattened tile index
+  int32_t b, h, tile_in_pair, len, nt, kind;
+};
+static_assert(sizeof(TileMeta) == 32, "stage record");
+
+__device__ __forceinline__ TileMeta meta_of(const Walk& w, int64_t t, int32_t kind) {
+  TileMeta m;
+  m.tile = t;
+  m.b = static_cast<int32_t>(w.b);
+  m.h = static_cast<int32_t>(w.h);
+  m.tile_in_pair = static_cast<int32_t>(w.tile);
+  m.len = w.len;
+  m.nt = static_cast<int32_t>(w.nt);
+  m.kind = kind;
+  return m;
+}
+
+__device__ __forceinline__ TileMeta meta_marker(int32_t kind) {
+  TileMeta m;
+  m.tile = -1;
+  m.b = m.h = m.tile_in_pair = m.len = m.nt = 0;
+  m.kind = kind;
+  return m;
+}
+
 template <int D, int kWarps, int kMB, int kStages, bool kTma>
 struct StreamCfg {
   static constexpr int kTT = 16 * kWarps * kMB;  // tokens per tile
@@ -145,12 +230,18 @@ struct StreamCfg {
   static constexpr int kFlushAccBytes = kWarps * kMaxGroup * D * 4;
   static constexpr int kFlushMlBytes = kWarps * kMaxGroup * 2 * 4;
   static constexpr int kBarBytes = 2 * kRingStages * 8;
-  static constexpr int kMiscBytes = 48 * 8;
-  static constexpr int kSmemBytes =
-      1024 + kRingBytes + kFlushAccBytes + kFlushMlBytes + kBarBytes + kMiscBytes;
+  static constexpr int kMetaBytes = kRingStages * 32;
+  static constexpr int kTableBytes = (kMaxTableBatches + 1) * 8;
+  static constexpr int kMiscBytes = 64 * 8;
+  static constexpr int kSmemBytes = 1024 + kRingBytes + kFlushAccBytes + kFlushMlBytes +
+                                    kBarBytes + kMetaBytes + kTableBytes + kMiscBytes;
+  // Heads one consumer warp merges (warp w takes heads w, w + kWarps, ...).
+  static constexpr int kHeadsPerWarp = (kMaxGroup + kWarps - 1) / kWarps;
   static_assert(D == 64 || D == 128, "head_dim");
   static_assert(kTT <= 256, "TMA box rows");
   static_assert(kBoxBytes % 1024 == 0, "128B-swizzle boxes must stay 1024-byte aligned");
+  // The merge's slot list reuses the flush accumulator region.
+  static constexpr int kMergeList = kFlushAccBytes / 4;
 };
 
 // Byte offset of the 16-byte chunk `chunk` (0..7) of row `row` inside a
@@ -166,6 +257,7 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   using C = StreamCfg<D, kWarps, kMB, kStages, kTma>;
   constexpr int TT = C::kTT;
   constexpr int kSlabs = D / 16;
+  constexpr int kCT = C::kConsumerThreads;
 
   extern __shared__ uint8_t smem_raw[];
   // 128-byte-swizzled TMA boxes need 1024-byte aligned shared addresses.
@@ -175,80 +267,26 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   float* fl_m = fl_acc + kWarps * kMaxGroup * D;                    // [kWarps][8]
   float* fl_l = fl_m + kWarps * kMaxGroup;                          // [kWarps][8]
   uint64_t* bars = reinterpret_cast<uint64_t*>(fl_l + kWarps * kMaxGroup);
-  int64_t* misc = reinterpret_cast<int64_t*>(bars + 2 * C::kRingStages);
-  // misc[0..32]: scan scratch; misc[40]: start batch; misc[41]: its tile base;
-  // misc[42]: abort flag (int)
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 42);
+  TileMeta* meta = reinterpret_cast<TileMeta*>(bars + 2 * C::kRingStages);
+  int64_t* table = reinterpret_cast<int64_t*>(meta + C::kRingStages);  // [B+1] varlen
+  int64_t* misc = table + kMaxTableBatches + 1;
+  // misc[0..32]: scan scratch; misc[40..43]: batches / bases of the first and
+  // last tile; misc[44]: dynamic slot of a thief flush; misc[46]: broadcast
+  // flag; misc[47]: dynamic slots in use; misc[48]: merge segment count;
+  // misc[50]: abort flag
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 50);
+  // merge slot list, aliased on fl_acc (see StreamCfg)
+  int32_t* mg_list = reinterpret_cast<int32_t*>(fl_acc);
 
-  // The combine kernel is launched with programmatic stream serialisation;
-  // it blocks in griddepcontrol.wait until this grid has completed.
+  // Let the next kernel in the stream launch early; it must wait for this
+  // grid (griddepcontrol.wait) before touching memory, as this one does.
   griddep_launch_dependents();
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t B = p.batch, Hkv = p.kv_heads, S = p.kv_len;
   const int64_t nc = gridDim.x, c = blockIdx.x;
-
-  // ------------------------------------------------------------ tile range
-  int64_t nt_total, t0, t1;
-  Walk start;
-  start.tile = 0;
-  if (p.seqlens == nullptr) {
-    const int64_t nt = (S + TT - 1) / TT;
-    nt_total = B * Hkv * nt;
-    t0 = c * nt_total / nc;
-    t1 = (c + 1) * nt_total / nc;
-    if (t0 >= t1) return;
-    const int64_t pair = t0 / nt;
-    start.b = pair / Hkv;
-    start.h = pair - start.b * Hkv;
-    start.tile = t0 - pair * nt;
-    start.nt = nt;
-    start.len = static_cast<int32_t>(S);
-  } else {
-    // Pass 1: total tiles.  Pass 2: the batch holding tile t0 (and, in CTA 0,
-    // the per-batch tile prefix the combine kernel reads).
-    int64_t local = 0;
-    for (int64_t b = tid; b < B; b += blockDim.x)
-      local += Hkv * ((static_cast<int64_t>(clamped_len(p, b)) + TT - 1) / TT);
-    int64_t total = 0;
-    block_inclusive_scan(local, misc, total);
-    nt_total = total;
-    t0 = nt_total > 0 ? c * nt_total / nc : 0;
-    t1 = nt_total > 0 ? (c + 1) * nt_total / nc : 0;
-    if (tid == 0) misc[40] = -1;
-    __syncthreads();
-    const bool writer = (c == 0);
-    if (t0 < t1 || writer) {
-      int64_t running = 0;
-      for (int64_t base = 0; base < B; base += blockDim.x) {
-        const int64_t b = base + tid;
-        const int64_t x =
-            b < B ? Hkv * ((static_cast<int64_t>(clamped_len(p, b)) + TT - 1) / TT) : 0;
-        int64_t chunk_total = 0;
-        const int64_t incl = block_inclusive_scan(x, misc, chunk_total);
-        const int64_t excl = running + incl - x;
-        if (b < B) {
-          if (writer) p.ws_cum[b] = excl;
-          if (x > 0 && excl <= t0 && t0 < excl + x) {
-            misc[40] = b;
-            misc[41] = excl;
-          }
-        }
-        running += chunk_total;
-        __syncthreads();
-        if (!writer && misc[40] >= 0) break;
-      }
-      if (writer && tid == 0) p.ws_cum[B] = running;
-    }
-    if (t0 >= t1) return;
-    const int64_t b0 = misc[40];
-    const int64_t base0 = misc[41];
-    walk_set_batch(start, p, b0, TT);
-    const int64_t r = t0 - base0;
-    start.h = r / start.nt;
-    start.tile = r - start.h * start.nt;
-  }
-  const int64_t n_tiles = t1 - t0;
+  const int64_t P = B * Hkv;
+  const int G = p.group;
 
   // ------------------------------------------------------------ barriers
   const uint32_t bar_base = smem_u32(bars);
@@ -267,23 +305,140 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
     }
   }
   __syncthreads();
+  // No global memory is touched before the previous grid in the stream is done.
+  griddep_wait();
+
+  // ------------------------------------------------------------ tile range
+  const int64_t nt_uniform = (S + TT - 1) / TT;
+  int64_t nt_total, t0, t1;
+  Walk first_w, last_w;  // tiles t0 and t1 - 1 (valid when t0 < t1)
+  bool have_table = false;
+  if (p.seqlens == nullptr) {
+    nt_total = P * nt_uniform;
+    t0 = c * nt_total / nc;
+    t1 = (c + 1) * nt_total / nc;
+    if (t0 < t1) {
+      const int64_t b0 = t0 / nt_uniform / Hkv, b1 = (t1 - 1) / nt_uniform / Hkv;
+      walk_locate(first_w, p, b0, b0 * Hkv * nt_uniform, t0, TT);
+      walk_locate(last_w, p, b1, b1 * Hkv * nt_uniform, t1 - 1, TT);
+    }
+  } else {
+    // Pass 1: total tiles.  Pass 2: per-batch tile prefix (kept in shared
+    // memory when the batch is small) and the batches holding tiles t0 and
+    // t1 - 1.  CTA 0 also writes the rows of empty sequences.
+    int64_t local = 0;
+    for (int64_t b = tid; b < B; b += blockDim.x) local += Hkv * tiles_of(clamped_len(p, b), TT);
+    int64_t total = 0;
+    block_inclusive_scan(local, misc, total);
+    nt_total = total;
+    t0 = nt_total > 0 ? c * nt_total / nc : 0;
+    t1 = nt_total > 0 ? (c + 1) * nt_total / nc : 0;
+    have_table = B <= kMaxTableBatches;
+    if (tid == 0) misc[40] = misc[42] = -1;
+    __syncthreads();
+    if (have_table || t0 < t1) {
+      int64_t running = 0;
+      for (int64_t base = 0; base < B; base += blockDim.x) {
+        const int64_t b = base + tid;
+        const int64_t x = b < B ? Hkv * tiles_of(clamped_len(p, b), TT) : 0;
+        int64_t chunk_total = 0;
+        const int64_t incl = block_inclusive_scan(x, misc, chunk_total);
+        const int64_t excl = running + incl - x;
+        if (b < B) {
+          if (have_table) table[b] = excl;
+          if (x > 0 && excl <= t0 && t0 < excl + x) {
+            misc[40] = b;
+            misc[41] = excl;
+          }
+          if (x > 0 && excl <= t1 - 1 && t1 - 1 < excl + x) {
+            misc[42] = b;
+            misc[43] = excl;
+          }
+        }
+        running += chunk_total;
+        __syncthreads();
+        if (!have_table && misc[40] >= 0 && misc[42] >= 0) break;
+      }
+      if (tid == 0 && have_table) table[B] = running;
+    }
+    __syncthreads();
+    if (t0 < t1) {
+      walk_locate(first_w, p, misc[40], misc[41], t0, TT);
+      walk_locate(last_w, p, misc[42], misc[43], t1 - 1, TT);
+    }
+    if (c == 0) {  // empty sequences: zero output rows / empty states
+      const int64_t Hq = Hkv * G;
+      for (int64_t b = tid; b < B; b += blockDim.x) {
+        if (clamped_len(p, b) != 0) continue;
+        for (int64_t row = b * Hq; row < (b + 1) * Hq; ++row) {
+          for (int d = 0; d < D; ++d) {
+            if (p.partial_mode)
+              p.state_acc[row * D + d] = 0.f;
+            else
+              p.out[row * D + d] = __float2bfloat16_rn(0.f);
+          }
+          if (p.partial_mode) {
+            p.state_ml[2 * row] = neg_inf();
+            p.state_ml[2 * row + 1] = 0.f;
+          }
+        }
+      }
+    }
+  }
+  // Thieves decode arbitrary tiles, which needs the uniform layout or the table.
+  const bool steal = kTma && p.steal && (p.seqlens == nullptr || have_table) && nt_total > 0;
+  auto steal_on = [&](int64_t) { return steal; };
+  // Processing order of a CTA's range [s, e) of n tiles: when the last pair
+  // of the range continues into the next CTA's range, its part ("rot"
+  // tiles) comes first, so both CTAs sharing the pair commit it early and
+  // its merge overlaps the stream; then [s, e - rot) in order.  Positions
+  // [0, n - n/claim_divisor) are static; with stealing the remaining
+  // positions are claimed through the CTA's counter, by the owner or by
+  // thieves.
+  auto rot_of = [&](int64_t n, const Walk& lw) -> int64_t {
+    const int64_t r = (lw.tile + 1 < lw.nt) ? (lw.tile + 1 < n ? lw.tile + 1 : n) : 0;
+    return r == n ? 0 : r;
+  };
+  auto dyn_size_of = [&](int64_t n) -> int64_t { return steal_on(n) ? n / p.claim_divisor : 0; };
+  auto tile_at = [&](int64_t s_v, int64_t e_v, int64_t rot, int64_t pos) -> int64_t {
+    return pos < rot ? e_v - rot + pos : s_v + pos - rot;
+  };
+
+  // Decode any tile t (uniform layout or varlen table).
+  auto locate = [&](int64_t t, Walk& w) {
+    if (p.seqlens == nullptr) {
+      const int64_t b = t / nt_uniform / Hkv;
+      walk_locate(w, p, b, b * Hkv * nt_uniform, t, TT);
+    } else {
+      int64_t lo = 0, hi = B;  // table[lo] <= t < table[hi]
+      while (hi - lo > 1) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (table[mid] <= t)
+          lo = mid;
+        else
+          hi = mid;
+      }
+      walk_locate(w, p, lo, table[lo], t, TT);
+    }
+  };
 
   // ------------------------------------------------------------ producer
   if constexpr (kTma) {
     if (warp == kWarps) {
-      if (lane == 0) {
-        Walk w = start;
-        for (int64_t k = 0; k < n_tiles; ++k) {
-          const int s = static_cast<int>(k % kStages);
-          if (k >= kStages) {
-            if (!mbar_wait(empty_bar(s), static_cast<uint32_t>((k / kStages) - 1) & 1u,
-                           abort_flag))
-              break;
-          }
+      int64_t k = 0;  // stage sequence number (lane 0)
+      bool ok = true;
+      // Lane 0: fill stage k with `m` (and its tile, if it is one).
+      auto issue = [&](const TileMeta& m) -> bool {
+        const int s = static_cast<int>(k % kStages);
+        if (k >= kStages &&
+            !mbar_wait(empty_bar(s), static_cast<uint32_t>((k / kStages) - 1) & 1u, abort_flag))
+          return false;
+        meta[s] = m;
+        if (m.kind == kMetaOwn || m.kind == kMetaStolen) {
           mbar_arrive_expect_tx(full_bar(s), C::kStageBytes);
           uint8_t* st = ring + static_cast<size_t>(s) * C::kStageBytes;
-          const int y = static_cast<int>(w.tile * TT);
-          const int z = static_cast<int>(w.b * Hkv + w.h);
+          const int y = m.tile_in_pair * TT;
+          const int z = static_cast<int>(m.b * Hkv + m.h);
 #pragma unroll
           for (int h = 0; h < C::kHalves; ++h)
             tma_load_3d(smem_u32(st + h * C::kBoxBytes), &tm_k, h * 64, y, z, full_bar(s));
@@ -291,16 +446,131 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
           for (int h = 0; h < C::kHalves; ++h)
             tma_load_3d(smem_u32(st + (C::kHalves + h) * C::kBoxBytes), &tm_v, h * 64, y, z,
                         full_bar(s));
-          walk_next(w, p, TT);
+        } else {
+          mbar_arrive(full_bar(s));
+        }
+        ++k;
+        return true;
+      };
+
+      // Own phase: the static positions in order, then the claimable ones one
+      // claim at a time (the next claim is in flight while the current tile
+      // is issued).  One walk cursor per contiguous part of the order.
+      if (lane == 0) {
+        if (t0 < t1) {
+          const int64_t n = t1 - t0;
+          const int64_t rot = rot_of(n, last_w);
+          const int64_t n_dyn = dyn_size_of(n);
+          const int64_t n_stat = n - n_dyn;
+          Walk rw = last_w;  // rotated part [t1 - rot, t1)
+          rw.tile -= rot > 0 ? rot - 1 : 0;
+          int64_t rw_t = t1 - (rot > 0 ? rot : 1);
+          Walk nw = first_w;  // in-order part [t0, t1 - rot)
+          int64_t nw_t = t0;
+          auto issue_pos = [&](int64_t pos) -> bool {
+            const int64_t tt = tile_at(t0, t1, rot, pos);
+            Walk* cur = pos < rot ? &rw : &nw;
+            int64_t* cur_t = pos < rot ? &rw_t : &nw_t;
+            while (*cur_t < tt) {
+              walk_next(*cur, p, TT);
+              ++*cur_t;
+            }
+            return issue(meta_of(*cur, tt, kMetaOwn));
+          };
+          // A claim is valid while front + back < n_dyn (same atomic word).
+          auto valid = [&](unsigned long long w) {
+            return static_cast<int64_t>(w & 0xffffffffull) + static_cast<int64_t>(w >> 32) < n_dyn;
+          };
+          unsigned long long claim = n_dyn > 0 ? atomicAdd(p.ws_claims + c, 1ull) : 0ull;
+          for (int64_t pos = 0; pos < n_stat && ok; ++pos) ok = issue_pos(pos);
+          while (ok && n_dyn > 0 && valid(claim)) {
+            const unsigned long long next = atomicAdd(p.ws_claims + c, 1ull);
+            ok = issue_pos(n_stat + static_cast<int64_t>(claim & 0xffffffffull));
+            claim = next;
+          }
+        }
+        if (ok) ok = issue(meta_marker(kMetaEndOwn));
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+
+      // Steal phase: take up to kStealChunk positions from the back of the
+      // claimable part of the CTA with the most unclaimed positions.
+      if (steal && ok) {
+        int steals = 0;
+        const int max_steals = p.max_steals < kMaxSteals ? p.max_steals : kMaxSteals;
+        for (int attempt = 0; attempt < 4 * nc + 8 && steals < max_steals; ++attempt) {
+          int64_t best_rem = 0;
+          int64_t best_v = -1;
+          for (int64_t v = lane; v < nc; v += 32) {
+            const int64_t s_v = v * nt_total / nc, e_v = (v + 1) * nt_total / nc;
+            const int64_t size_v = dyn_size_of(e_v - s_v);
+            const unsigned long long w = __ldcv(p.ws_claims + v);
+            const int64_t rem = size_v - static_cast<int64_t>(w & 0xffffffffull) -
+                                static_cast<int64_t>(w >> 32);
+            if (rem > best_rem) {
+              best_rem = rem;
+              best_v = v;
+            }
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            const int64_t r2 = __shfl_xor_sync(0xffffffffu, best_rem, o);
+            const int64_t v2 = __shfl_xor_sync(0xffffffffu, best_v, o);
+            if (r2 > best_rem || (r2 == best_rem && v2 > best_v)) {
+              best_rem = r2;
+              best_v = v2;
+            }
+          }
+          if (best_rem < kStealMinRemaining) break;
+          const int64_t s_v = best_v * nt_total / nc, e_v = (best_v + 1) * nt_total / nc;
+          const int64_t n_v = e_v - s_v;
+          const int64_t size_v = dyn_size_of(n_v);
+          int64_t got = 0, back = 0;  // positions [n_v - back - got, n_v - back)
+          if (lane == 0) {
+            unsigned long long cur = __ldcv(p.ws_claims + best_v);
+            for (int tries = 0; tries < 8; ++tries) {
+              const int64_t f = static_cast<int64_t>(cur & 0xffffffffull);
+              const int64_t bk = static_cast<int64_t>(cur >> 32);
+              const int64_t rem = size_v - f - bk;
+              if (rem < kStealMinRemaining) break;
+              int64_t take = rem / 2;
+              take = take > kStealChunk ? kStealChunk : take;
+              const unsigned long long want = cur + (static_cast<unsigned long long>(take) << 32);
+              const unsigned long long seen = atomicCAS(p.ws_claims + best_v, cur, want);
+              if (seen == cur) {
+                got = take;
+                back = bk;
+                break;
+              }
+              cur = seen;
+            }
+          }
+          got = __shfl_sync(0xffffffffu, got, 0);
+          back = __shfl_sync(0xffffffffu, back, 0);
+          if (got == 0) continue;
+          ++steals;
+          if (lane == 0) {
+            Walk lw;
+            locate(e_v - 1, lw);
+            const int64_t rot_v = rot_of(n_v, lw);
+            for (int64_t i = 0; i < got && ok; ++i) {
+              const int64_t tt = tile_at(s_v, e_v, rot_v, n_v - back - got + i);
+              Walk w;
+              locate(tt, w);
+              ok = issue(meta_of(w, tt, kMetaStolen));
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
         }
       }
+      if (lane == 0 && ok) issue(meta_marker(kMetaEndAll));
       return;
     }
   }
 
   // ------------------------------------------------------------ consumers
   const int g = lane >> 2, t = lane & 3;
-  const int G = p.group;
   const uint16_t* q16 = reinterpret_cast<const uint16_t*>(p.q);
   const uint16_t* k16 = reinterpret_cast<const uint16_t*>(p.k);
   const uint16_t* v16 = reinterpret_cast<const uint16_t*>(p.v);
@@ -330,42 +600,340 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
     l_run[0] = l_run[1] = 0.f;
   };
 
-  Walk w = start;
-  int64_t seg_first_tile = w.tile;
-  load_q(w.b * Hkv + w.h);
+  auto bar = [&]() { named_barrier_sync(1, kCT); };
+  // Dynamic slots handed out so far, never more than the workspace holds.
+  auto dyn_in_use = [&]() -> int64_t {
+    const int64_t n = static_cast<int64_t>(__ldcg(p.ws_counters));
+    return n < p.dyn_capacity ? n : p.dyn_capacity;
+  };
+
+  // Merge every committed segment of pair q and write its output.  Called by
+  // all consumer threads of the CTA whose commit completed the pair.  The
+  // segment slots (owners first_cta..last_cta, then every dynamic slot
+  // tagged with q, found by a scan shared by all threads) are listed in
+  // shared memory; each warp merges its heads with one segment per lane for
+  // the weights and one row per load for the sums.
+  auto merge_pair = [&](int64_t q, int64_t first, int64_t last, int64_t n_thieves) {
+    __threadfence();
+    constexpr int kPer = D / 32;
+    float mrun[C::kHeadsPerWarp], lrun[C::kHeadsPerWarp], o[C::kHeadsPerWarp][kPer];
+#pragma unroll
+    for (int hi = 0; hi < C::kHeadsPerWarp; ++hi) {
+      mrun[hi] = neg_inf();
+      lrun[hi] = 0.f;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) o[hi][i] = 0.f;
+    }
+    // Thief segments are found by their tags; without thieves no scan is needed.
+    if (n_thieves > 0) {
+      if (tid == 0) misc[47] = dyn_in_use();
+      bar();
+    }
+    const int64_t n_tag = n_thieves > 0 ? misc[47] : 0;
+    const int64_t n_owner = last - first + 1;  // <= Nc
+    const int64_t per_pass = C::kMergeList - n_owner;
+    const int64_t passes = n_tag > 0 ? (n_tag + per_pass - 1) / per_pass : 1;
+    for (int64_t r = 0; r < passes; ++r) {
+      if (tid == 0) {
+        int n = 0;
+        if (r == 0)
+          for (int64_t cc = first; cc <= last; ++cc)
+            if (cc * nt_total / nc != (cc + 1) * nt_total / nc)
+              mg_list[n++] = static_cast<int32_t>(cc + q);
+        misc[48] = n;
+      }
+      bar();
+      const int64_t d_end = (r + 1) * per_pass < n_tag ? (r + 1) * per_pass : n_tag;
+      for (int64_t d = r * per_pass + tid; d < d_end; d += kCT)
+        if (__ldcg(p.ws_slot_pair + d) == static_cast<uint32_t>(q + 1))
+          mg_list[atomicAdd(reinterpret_cast<int*>(misc + 48), 1)] = static_cast<int32_t>(nc + P + d);
+      bar();
+      const int n = static_cast<int>(misc[48]);
+#pragma unroll
+      for (int hi = 0; hi < C::kHeadsPerWarp; ++hi) {
+        const int hd = warp + hi * kWarps;
+        if (hd >= G) break;
+        // Four segments at a time: their (m, l) and this lane's slice of
+        // their accumulator rows are loaded together (one round trip), then
+        // folded into the running state.
+        for (int j0 = 0; j0 < n; j0 += 4) {
+          float mj[4], lj[4], x[4][kPer];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            mj[u] = neg_inf();
+            lj[u] = 0.f;
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) x[u][i] = 0.f;
+            if (j0 + u < n) {
+              const int64_t srow = static_cast<int64_t>(mg_list[j0 + u]) * G + hd;
+              const float2 ml2 = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + 2 * srow));
+              mj[u] = ml2.x;
+              lj[u] = ml2.y;
+              const float* row = p.ws_acc + srow * D + lane * kPer;
+              if constexpr (kPer == 4) {
+                const float4 v4 = __ldcg(reinterpret_cast<const float4*>(row));
+                x[u][0] = v4.x; x[u][1] = v4.y; x[u][2] = v4.z; x[u][3] = v4.w;
+              } else {
+                const float2 v2 = __ldcg(reinterpret_cast<const float2*>(row));
+                x[u][0] = v2.x; x[u][1] = v2.y;
+              }
+            }
+          }
+          float mnew = mrun[hi];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (lj[u] > 0.f) mnew = fmaxf(mnew, mj[u]);
+          const float mu = mnew == neg_inf() ? 0.f : mnew;
+          const float alpha = fast_exp2(mrun[hi] - mu);
+          lrun[hi] *= alpha;
+#pragma unroll
+          for (int i = 0; i < kPer; ++i) o[hi][i] *= alpha;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            // empty owner states (l = 0) hold no accumulator; skip them
+            const float w = lj[u] > 0.f ? fast_exp2(mj[u] - mu) : 0.f;
+            lrun[hi] += w * lj[u];
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) o[hi][i] += w > 0.f ? w * x[u][i] : 0.f;
+          }
+          mrun[hi] = mnew;
+        }
+      }
+      bar();  // the list is refilled next pass
+    }
+#pragma unroll
+    for (int hi = 0; hi < C::kHeadsPerWarp; ++hi) {
+      const int hd = warp + hi * kWarps;
+      if (hd >= G) break;
+      const int64_t row = q * G + hd;
+      const float L = lrun[hi];
+      if (p.partial_mode) {
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) p.state_acc[row * D + lane * kPer + i] = o[hi][i];
+        if (lane == 0) {
+          p.state_ml[2 * row] = mrun[hi] * kLn2;
+          p.state_ml[2 * row + 1] = L;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kPer; ++i)
+          p.out[row * D + lane * kPer + i] = __float2bfloat16_rn(L > 0.f ? o[hi][i] / L : 0.f);
+      }
+    }
+  };
+
+  // Commit `add` for pair q (after this CTA's segment of q is written) and
+  // merge the pair if this commit completes it.
+  auto commit = [&](int64_t q, int64_t toff, int64_t nt_q, unsigned long long add) {
+    __threadfence();
+    bar();
+    const int64_t first = cta_of_tile(toff, nt_total, nc);
+    const int64_t last = cta_of_tile(toff + nt_q - 1, nt_total, nc);
+    if (tid == 0) {
+      int64_t owners = last - first + 1;
+      if (nc > nt_total) {  // some CTAs have an empty range
+        owners = 0;
+        for (int64_t cc = first; cc <= last; ++cc)
+          owners += (cc * nt_total / nc != (cc + 1) * nt_total / nc);
+      }
+      const unsigned long long expected =
+          (static_cast<unsigned long long>(owners) << 48) + static_cast<unsigned long long>(nt_q);
+      const unsigned long long now = atomicAdd(p.ws_done + q, add) + add;
+      const unsigned long long thieves = (now >> 32) & 0xffffull;
+      misc[46] = ((now & ~(0xffffull << 32)) == expected) ? static_cast<int64_t>(thieves) + 1 : 0;
+    }
+    bar();
+    const int64_t done = misc[46];  // 0: not complete; else 1 + thief segments
+    if (done) merge_pair(q, first, last, done - 1);
+  };
+
+  // Owner slots of pairs [q0, q1] whose tiles were all stolen: empty states,
+  // committed as owners with no tiles.
+  auto flush_empty = [&](int64_t q0, int64_t q1) {
+    for (int64_t q = q0; q <= q1; ++q) {
+      const int64_t b = q / Hkv, h = q - b * Hkv;
+      const int64_t nt_q = tiles_of(clamped_len(p, b), TT);
+      // Empty sequences have no tiles and no owner (CTA 0 wrote their rows);
+      // pairs are skipped only when stealing is on, which implies the table.
+      if (nt_q == 0 || (p.seqlens != nullptr && !have_table)) continue;
+      if (tid < G) {
+        const int64_t srow = (c + q) * G + tid;
+        p.ws_ml[2 * srow] = neg_inf();
+        p.ws_ml[2 * srow + 1] = 0.f;
+      }
+      const int64_t toff = p.seqlens == nullptr ? q * nt_uniform : table[b] + h * nt_q;
+      commit(q, toff, nt_q, 1ull << 48);
+    }
+  };
+
+  // Merge the kWarps states of `pair` and write them: directly when this
+  // owner processed the whole pair, else to a slot followed by a commit.
+  auto flush = [&](int64_t pair, bool thief, int64_t toff, int64_t nt_q, int64_t tiles) {
+    const bool complete = !thief && tiles == nt_q;
+    float lr0 = l_run[0], lr1 = l_run[1];
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      lr0 += __shfl_xor_sync(0xffffffffu, lr0, o);
+      lr1 += __shfl_xor_sync(0xffffffffu, lr1, o);
+    }
+    if (g == 0) {
+      fl_m[warp * kMaxGroup + 2 * t] = m_run[0];
+      fl_m[warp * kMaxGroup + 2 * t + 1] = m_run[1];
+      fl_l[warp * kMaxGroup + 2 * t] = lr0;
+      fl_l[warp * kMaxGroup + 2 * t + 1] = lr1;
+    }
+    float* wa = fl_acc + warp * kMaxGroup * D;
+#pragma unroll
+    for (int j = 0; j < kSlabs; ++j) {
+      wa[(2 * t) * D + 16 * j + g] = acc[j][0];
+      wa[(2 * t + 1) * D + 16 * j + g] = acc[j][1];
+      wa[(2 * t) * D + 16 * j + 8 + g] = acc[j][2];
+      wa[(2 * t + 1) * D + 16 * j + 8 + g] = acc[j][3];
+    }
+    if (thief && tid == 0) {
+      const uint32_t d = atomicAdd(p.ws_counters, 1u);
+      if (d < p.dyn_capacity) {
+        p.ws_slot_pair[d] = static_cast<uint32_t>(pair + 1);
+        misc[44] = nc + P + d;
+      } else {  // cannot happen with a zeroed header (the capacity bounds the claims)
+        atomicOr(&g_adb_error_flag, kErrWorkspace);
+        misc[44] = -1;
+      }
+    }
+    bar();
+    const int64_t slot = thief ? misc[44] : c + pair;
+    if (slot < 0) {  // uniform: every thread read the same value
+      bar();
+      reset_state();
+      return;
+    }
+    for (int e = tid; e < G * D; e += kCT) {
+      const int hd = e / D, d = e - hd * D;
+      float M = neg_inf();
+#pragma unroll
+      for (int ww = 0; ww < kWarps; ++ww) M = fmaxf(M, fl_m[ww * kMaxGroup + hd]);
+      const float Mu = M == neg_inf() ? 0.f : M;
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < kWarps; ++ww) {
+        const float f = fast_exp2(fl_m[ww * kMaxGroup + hd] - Mu);
+        L += f * fl_l[ww * kMaxGroup + hd];
+        O += f * fl_acc[(ww * kMaxGroup + hd) * D + d];
+      }
+      const int64_t row = pair * G + hd;
+      if (complete && !p.partial_mode) {
+        p.out[row * D + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+      } else if (complete) {
+        p.state_acc[row * D + d] = O;
+        if (d == 0) {
+          p.state_ml[2 * row] = M * kLn2;
+          p.state_ml[2 * row + 1] = L;
+        }
+      } else {
+        const int64_t srow = slot * G + hd;
+        p.ws_acc[srow * D + d] = O;
+        if (d == 0) {
+          p.ws_ml[2 * srow] = M;
+          p.ws_ml[2 * srow + 1] = L;
+        }
+      }
+    }
+    bar();  // fl_* reads done before the merge scratch (aliased) is used
+    if (!complete)
+      commit(pair, toff, nt_q,
+             (thief ? (1ull << 32) : (1ull << 48)) + static_cast<unsigned long long>(tiles));
+    reset_state();
+  };
+
+  const int64_t pair_first = t0 < t1 ? first_w.b * Hkv + first_w.h : 0;
+  const int64_t pair_last = t0 < t1 ? last_w.b * Hkv + last_w.h : -1;
+  // The own phase visits the rotated pair (if any) first, then pairs in
+  // increasing order; owner slots of pairs it never saw get empty states.
+  const int64_t rot_pair = (t0 < t1 && rot_of(t1 - t0, last_w) > 0) ? pair_last : -1;
+  int64_t inc_next = pair_first;
+  const int64_t inc_last = rot_pair >= 0 ? pair_last - 1 : pair_last;
+  int64_t cur_pair = -1, cur_count = 0, cur_nt = 0, cur_toff = 0;
+  bool thief_phase = false;
+  Walk gen = first_w;  // generic path: next own tile
+  int64_t gen_t = t0;
+  bool gen_end_own = false;
   reset_state();
 
-  for (int64_t k = 0; k < n_tiles; ++k) {
+  for (int64_t k = 0;; ++k) {
     const int s = kTma ? static_cast<int>(k % kStages) : 0;
     const uint8_t* st = ring + static_cast<size_t>(s) * C::kStageBytes;
-    const int64_t tile_tok0 = w.tile * TT;
-    const int valid =
-        static_cast<int>(min(static_cast<int64_t>(TT), static_cast<int64_t>(w.len) - tile_tok0));
-    bool have_data = true;
+    TileMeta m;
     if constexpr (kTma) {
-      have_data = mbar_wait(full_bar(s), static_cast<uint32_t>(k / kStages) & 1u, abort_flag);
+      if (!mbar_wait(full_bar(s), static_cast<uint32_t>(k / kStages) & 1u, abort_flag)) break;
+      m = meta[s];
     } else {
-      // Generic path for K/V that are not 16-byte aligned: every warp copies
-      // its own rows with 2-byte loads into the same swizzled layout.
-      __syncwarp();
-      uint8_t* dst = ring;
-      const int64_t row0 = (w.b * Hkv + w.h) * S + tile_tok0;
-      for (int e = lane; e < 16 * kMB * D; e += 32) {
-        const int r = warp * 16 * kMB + e / D, col = e % D;
-        uint16_t kx = 0, vx = 0;
-        if (r < valid) {
-          kx = __ldg(k16 + (row0 + r) * D + col);
-          vx = __ldg(v16 + (row0 + r) * D + col);
+      // Generic path (K/V not 16-byte aligned): no producer and no stealing;
+      // every warp copies its own rows with 2-byte loads into the same
+      // swizzled layout.
+      if (gen_t < t1) {
+        m = meta_of(gen, gen_t, kMetaOwn);
+        __syncwarp();
+        uint8_t* dst = ring;
+        const int64_t row0 = (gen.b * Hkv + gen.h) * S + gen.tile * TT;
+        const int valid_rows =
+            static_cast<int>(min(static_cast<int64_t>(TT), gen.len - gen.tile * TT));
+        for (int e = lane; e < 16 * kMB * D; e += 32) {
+          const int r = warp * 16 * kMB + e / D, col = e % D;
+          uint16_t kx = 0, vx = 0;
+          if (r < valid_rows) {
+            kx = __ldg(k16 + (row0 + r) * D + col);
+            vx = __ldg(v16 + (row0 + r) * D + col);
+          }
+          const uint32_t off = swz128(r, (col & 63) >> 3) + (col & 7) * 2;
+          const int h = col >> 6;
+          *reinterpret_cast<uint16_t*>(dst + h * C::kBoxBytes + off) = kx;
+          *reinterpret_cast<uint16_t*>(dst + (C::kHalves + h) * C::kBoxBytes + off) = vx;
         }
-        const uint32_t off = swz128(r, (col & 63) >> 3) + (col & 7) * 2;
-        const int h = col >> 6;
-        *reinterpret_cast<uint16_t*>(dst + h * C::kBoxBytes + off) = kx;
-        *reinterpret_cast<uint16_t*>(dst + (C::kHalves + h) * C::kBoxBytes + off) = vx;
+        __syncwarp();
+        ++gen_t;
+        if (gen_t < t1) walk_next(gen, p, TT);
+      } else {
+        m = meta_marker(gen_end_own ? kMetaEndAll : kMetaEndOwn);
+        gen_end_own = true;
       }
-      __syncwarp();
     }
+    auto release = [&]() {
+      if constexpr (kTma) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar(s));
+      }
+    };
 
-    if (have_data) {
+    if (m.kind == kMetaEndOwn) {
+      release();
+      if (cur_pair >= 0) flush(cur_pair, false, cur_toff, cur_nt, cur_count);
+      flush_empty(inc_next, inc_last);
+      cur_pair = -1;
+      thief_phase = true;
+      continue;
+    }
+    if (m.kind == kMetaEndAll) {
+      release();
+      if (cur_pair >= 0) flush(cur_pair, true, cur_toff, cur_nt, cur_count);
+      break;
+    }
+    const int64_t pair = static_cast<int64_t>(m.b) * Hkv + m.h;
+    if (pair != cur_pair) {
+      if (cur_pair >= 0) flush(cur_pair, thief_phase, cur_toff, cur_nt, cur_count);
+      if (!thief_phase && pair != rot_pair) {
+        flush_empty(inc_next, pair - 1);
+        inc_next = pair + 1;
+      }
+      cur_pair = pair;
+      cur_count = 0;
+      cur_nt = m.nt;
+      cur_toff = m.tile - m.tile_in_pair;
+      load_q(pair);
+    }
+    const int valid = static_cast<int>(
+        min(static_cast<int64_t>(TT),
+            static_cast<int64_t>(m.len) - static_cast<int64_t>(m.tile_in_pair) * TT));
+    {
       const uint32_t kbase = smem_u32(st);
       const uint32_t vbase = kbase + C::kHalves * C::kBoxBytes;
       // ---- S^T = K . Q^T  (tokens x heads), two accumulation chains
@@ -453,175 +1021,35 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
         }
       }
     }
-    if constexpr (kTma) {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty_bar(s));
-    }
+    release();
+    ++cur_count;
+  }
 
-    // ---- segment end: merge the kWarps states and write the result
-    const bool last_in_pair = (w.tile == w.nt - 1);
-    if (last_in_pair || k == n_tiles - 1) {
-      const bool complete = (seg_first_tile == 0) && last_in_pair;
-      const int64_t pair = w.b * Hkv + w.h;
-      float lr0 = l_run[0], lr1 = l_run[1];
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        lr0 += __shfl_xor_sync(0xffffffffu, lr0, o);
-        lr1 += __shfl_xor_sync(0xffffffffu, lr1, o);
-      }
-      if (g == 0) {
-        fl_m[warp * kMaxGroup + 2 * t] = m_run[0];
-        fl_m[warp * kMaxGroup + 2 * t + 1] = m_run[1];
-        fl_l[warp * kMaxGroup + 2 * t] = lr0;
-        fl_l[warp * kMaxGroup + 2 * t + 1] = lr1;
-      }
-      float* wa = fl_acc + warp * kMaxGroup * D;
-#pragma unroll
-      for (int j = 0; j < kSlabs; ++j) {
-        wa[(2 * t) * D + 16 * j + g] = acc[j][0];
-        wa[(2 * t + 1) * D + 16 * j + g] = acc[j][1];
-        wa[(2 * t) * D + 16 * j + 8 + g] = acc[j][2];
-        wa[(2 * t + 1) * D + 16 * j + 8 + g] = acc[j][3];
-      }
-      named_barrier_sync(1, C::kConsumerThreads);
-      for (int e = tid; e < G * D; e += C::kConsumerThreads) {
-        const int hd = e / D, d = e - hd * D;
-        float M = neg_inf();
-#pragma unroll
-        for (int ww = 0; ww < kWarps; ++ww) M = fmaxf(M, fl_m[ww * kMaxGroup + hd]);
-        const float Mu = M == neg_inf() ? 0.f : M;
-        float L = 0.f, O = 0.f;
-#pragma unroll
-        for (int ww = 0; ww < kWarps; ++ww) {
-          const float f = fast_exp2(fl_m[ww * kMaxGroup + hd] - Mu);
-          L += f * fl_l[ww * kMaxGroup + hd];
-          O += f * fl_acc[(ww * kMaxGroup + hd) * D + d];
-        }
-        const int64_t row = pair * G + hd;
-        if (complete && !p.partial_mode) {
-          p.out[row * D + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
-        } else if (complete) {
-          p.state_acc[row * D + d] = O;
-          if (d == 0) {
-            p.state_ml[2 * row] = M * kLn2;
-            p.state_ml[2 * row + 1] = L;
-          }
-        } else {
-          const int64_t srow = (c + pair) * G + hd;
-          p.ws_acc[srow * D + d] = O;
-          if (d == 0) {
-            p.ws_ml[2 * srow] = M;
-            p.ws_ml[2 * srow + 1] = L;
-          }
-        }
-      }
-      named_barrier_sync(1, C::kConsumerThreads);
-      reset_state();
+  // ------------------------------------------------------------ exit
+  // The last CTA to finish resets the scheduler header for the next call.
+  __threadfence();
+  bar();
+  if (tid == 0) misc[46] = atomicAdd(p.ws_counters + 1, 1u) == static_cast<uint32_t>(nc - 1);
+  bar();
+  if (misc[46]) {
+    __threadfence();
+    if (tid == 0) misc[47] = dyn_in_use();
+    bar();
+    const int64_t n_dyn = misc[47];
+    for (int64_t i = tid; i < nc; i += kCT) p.ws_claims[i] = 0ull;
+    for (int64_t i = tid; i < P; i += kCT) p.ws_done[i] = 0ull;
+    for (int64_t i = tid; i < n_dyn; i += kCT) p.ws_slot_pair[i] = 0u;
+    bar();
+    if (tid == 0) {
+      p.ws_counters[0] = 0u;
+      p.ws_counters[1] = 0u;
     }
-    if (k + 1 < n_tiles) {
-      const int64_t old_pair = w.b * Hkv + w.h;
-      walk_next(w, p, TT);
-      const int64_t new_pair = w.b * Hkv + w.h;
-      if (new_pair != old_pair) {
-        load_q(new_pair);
-        seg_first_tile = w.tile;
-      }
-    }
-  }
-}
-
-// Merges the workspace segments of every split (pair, head) row.  One warp
-// per output row; rows whose pair lies inside one CTA were written by the
-// partial kernel and are skipped.  Replaces merge_splits
-// (csrc/decode.cu:169-184).
-template <int D>
-__global__ void __launch_bounds__(256) combine_segments_kernel(const DecodeParams p) {
-  griddep_wait();
-  constexpr int kPer = D / 32;
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int G = p.group;
-  const int64_t Hkv = p.kv_heads;
-  const int64_t P = p.batch * Hkv;
-  if (row >= P * G) return;
-  const int64_t pair = row / G;
-  const int hd = static_cast<int>(row - pair * G);
-  const int64_t b = pair / Hkv, h = pair - b * Hkv;
-  const int tt = p.tile_tokens;
-  int64_t nt, toff, nt_total;
-  if (p.seqlens == nullptr) {
-    nt = (p.kv_len + tt - 1) / tt;
-    toff = pair * nt;
-    nt_total = P * nt;
-  } else {
-    nt = (static_cast<int64_t>(clamped_len(p, b)) + tt - 1) / tt;
-    toff = p.ws_cum[b] + h * nt;
-    nt_total = p.ws_cum[p.batch];
-  }
-  float* out_acc = p.partial_mode ? p.state_acc + row * D : nullptr;
-  if (nt == 0) {  // empty sequence: zero output / empty state
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int d = lane * kPer + i;
-      if (p.partial_mode)
-        out_acc[d] = 0.f;
-      else
-        p.out[row * D + d] = __float2bfloat16_rn(0.f);
-    }
-    if (p.partial_mode && lane == 0) {
-      p.state_ml[2 * row] = neg_inf();
-      p.state_ml[2 * row + 1] = 0.f;
-    }
-    return;
-  }
-  const int64_t nc = p.num_ctas;
-  const int64_t first = cta_of_tile(toff, nt_total, nc);
-  const int64_t last = cta_of_tile(toff + nt - 1, nt_total, nc);
-  if (first == last) return;
-  // With variable lengths there can be more CTAs than tiles; CTAs with an
-  // empty range wrote no segment and are skipped.
-  auto empty_cta = [&](int64_t cc) { return cc * nt_total / nc == (cc + 1) * nt_total / nc; };
-  float M = neg_inf();
-  for (int64_t cc = first; cc <= last; ++cc)
-    if (!empty_cta(cc)) M = fmaxf(M, p.ws_ml[2 * ((cc + pair) * G + hd)]);
-  const float Mu = M == neg_inf() ? 0.f : M;
-  float L = 0.f, O[kPer];
-#pragma unroll
-  for (int i = 0; i < kPer; ++i) O[i] = 0.f;
-  for (int64_t cc = first; cc <= last; ++cc) {
-    if (empty_cta(cc)) continue;
-    const int64_t srow = (cc + pair) * G + hd;
-    const float f = fast_exp2(p.ws_ml[2 * srow] - Mu);
-    L += f * p.ws_ml[2 * srow + 1];
-    const float* src = p.ws_acc + srow * D + lane * kPer;
-    if constexpr (kPer == 4) {
-      const float4 x = *reinterpret_cast<const float4*>(src);
-      O[0] += f * x.x;
-      O[1] += f * x.y;
-      O[2] += f * x.z;
-      O[3] += f * x.w;
-    } else {
-      const float2 x = *reinterpret_cast<const float2*>(src);
-      O[0] += f * x.x;
-      O[1] += f * x.y;
-    }
-  }
-  if (p.partial_mode) {
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) out_acc[lane * kPer + i] = O[i];
-    if (lane == 0) {
-      p.state_ml[2 * row] = M * kLn2;
-      p.state_ml[2 * row + 1] = L;
-    }
-  } else {
-    __nv_bfloat16* dst = p.out + row * D + lane * kPer;
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) dst[i] = __float2bfloat16_rn(L > 0.f ? O[i] / L : 0.f);
   }
 }
 
 // Merges `parts` public partial states (m in natural units) per row into
-// BF16.  One warp per row.
+// BF16.  One warp per row.  Used for the cross-GPU merge of sequence shards
+// (replaces merge_splits, csrc/decode.cu:169-184).
 template <int D>
 __global__ void __launch_bounds__(256)
     merge_states_kernel(const float* __restrict__ acc, int64_t acc_stride,
@@ -633,7 +1061,10 @@ __global__ void __launch_bounds__(256)
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
   float M = neg_inf();
-  for (int64_t r = 0; r < parts; ++r) M = fmaxf(M, ml[r * ml_stride + 2 * row]);
+  for (int64_t r = lane; r < parts; r += 32)
+    if (ml[r * ml_stride + 2 * row + 1] > 0.f) M = fmaxf(M, ml[r * ml_stride + 2 * row]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   const float Mu = M == neg_inf() ? 0.f : M;
   float L = 0.f, O[kPer];
 #pragma unroll

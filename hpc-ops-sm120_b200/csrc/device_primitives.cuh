@@ -60,6 +60,7 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 __device__ int g_adb_error_flag = 0;
 
 constexpr int kErrWaitTimeout = 1;
+constexpr int kErrWorkspace = 2;  // a scheduler counter left its bounds (dirty header)
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far above any legitimate wait
 
 // Waits for the given phase parity of an mbarrier.  The wait is bounded: if

@@ -18,6 +18,14 @@
  * stream-ordered and may be captured in a CUDA graph, and concurrent calls on
  * different streams are independent as long as their workspaces differ.
  *
+ * Workspace: the first `header_bytes` of a workspace hold the scheduler state
+ * of one call.  It must be zero when a call starts, and every call that
+ * completes leaves it zero again.  Pass ADB_FLAG_HEADER_ZEROED when that is
+ * known to hold (a workspace zeroed once and then reused only by calls that
+ * are ordered on one stream); without the flag the library zeroes the header
+ * with one cudaMemsetAsync on the call's stream.  Calls that may run
+ * concurrently must use different workspaces.
+ *
  * Error convention: every function returns an adb_status; on failure a
  * message is kept in thread-local storage (adb_last_error).  Argument errors
  * are detected on the host before any launch, mirroring the TORCH_CHECKs at
@@ -38,6 +46,9 @@
 #ifdef __cplusplus
 extern "C" {
 #endif
+
+/* Flags of adb_decode / adb_decode_partial. */
+#define ADB_FLAG_HEADER_ZEROED 1u /* the workspace header is already zero */
 
 typedef enum adb_status {
   ADB_OK = 0,
@@ -60,13 +71,14 @@ ADB_API const char* adb_last_error(void);
 ADB_API int adb_check_device(int device);
 
 /* Bytes of device workspace adb_decode / adb_decode_partial need for this
- * problem on `device` (depends on the device's SM count).  `has_seqlens` is
- * non-zero when a per-sequence length array will be passed.  Replaces the
- * reference's internal `at::empty({heads, splits, D + 2})` partial buffer
+ * problem on `device` (depends on the device's SM count), and the size of its
+ * leading scheduler header (may be NULL).  `has_seqlens` is non-zero when a
+ * per-sequence length array will be passed.  Replaces the reference's
+ * internal `at::empty({heads, splits, D + 2})` partial buffer
  * (csrc/decode.cu:205). */
 ADB_API int adb_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv_heads,
-                              int64_t kv_len, int64_t head_dim, int has_seqlens,
-                              int device, size_t* bytes);
+                                      int64_t kv_len, int64_t head_dim, int has_seqlens,
+                                      int device, size_t* bytes, size_t* header_bytes);
 
 /* Full decode into a BF16 output [batch, q_heads, 1, head_dim].
  *   q        [batch, q_heads, 1, head_dim]       bf16, contiguous
@@ -76,15 +88,19 @@ ADB_API int adb_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv
  *            of 0 gives an all-zero output row, as the FP32 oracle does)
  *   out      [batch, q_heads, 1, head_dim]       bf16
  *   workspace at least adb_decode_workspace_size() bytes, 256-byte aligned
+ *   flags    ADB_FLAG_HEADER_ZEROED or 0 (see "Workspace" above)
  *   stream   cudaStream_t (NULL = legacy default stream)
+ * The whole decode is one kernel launch (plus the header memset when the flag
+ * is not given), launched with programmatic stream serialisation so that it
+ * can start while the previous kernel in the stream drains. 
  * Replaces attention_decode_cuda (csrc/decode.cu:223-258) and its launch path
  * decode_bf16_mma + merge_splits (csrc/decode.cu:70-211).  K/V pointers that
  * are not 16-byte aligned are accepted (slower fallback path), matching the
  * reference's unaligned dispatch (csrc/decode.cu:212-220). */
 ADB_API int adb_decode(const void* q, const void* k, const void* v, const int32_t* seqlens,
-               void* out, int64_t batch, int64_t q_heads, int64_t kv_heads,
-               int64_t kv_len, int64_t head_dim, void* workspace,
-               size_t workspace_bytes, int device, void* stream);
+                       void* out, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                       int64_t kv_len, int64_t head_dim, void* workspace,
+                       size_t workspace_bytes, unsigned flags, int device, void* stream);
 
 /* Partial decode for sequence sharding: instead of the normalised output it
  * writes, per query-head row r = b * q_heads + hq,
@@ -95,10 +111,11 @@ ADB_API int adb_decode(const void* q, const void* k, const void* v, const int32_
  * The state layout is the reference's split partial (acc[D], m, l)
  * (csrc/decode.cu:127-129,160), kept as two arrays. */
 ADB_API int adb_decode_partial(const void* q, const void* k, const void* v,
-                       const int32_t* seqlens, float* acc, float* ml,
-                       int64_t batch, int64_t q_heads, int64_t kv_heads,
-                       int64_t kv_len, int64_t head_dim, void* workspace,
-                       size_t workspace_bytes, int device, void* stream);
+                               const int32_t* seqlens, float* acc, float* ml,
+                               int64_t batch, int64_t q_heads, int64_t kv_heads,
+                               int64_t kv_len, int64_t head_dim, void* workspace,
+                               size_t workspace_bytes, unsigned flags, int device,
+                               void* stream);
 
 /* Merges `parts` partial states per row into BF16 output rows:
  *   M = max_r m_r,  O = sum_r e^(m_r - M) acc_r / sum_r e^(m_r - M) l_r.

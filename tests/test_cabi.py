@@ -61,14 +61,14 @@ def test_workspace_query_validates_shapes_on_host(shape, status, pattern):
         pytest.skip("valid shape: the query would touch the device")
     lib = _lib.load_library()
     out = ctypes.c_size_t(0)
-    rc = lib.adb_decode_workspace_size(*shape, 0, 0, ctypes.byref(out))
+    rc = lib.adb_decode_workspace_size(*shape, 0, 0, ctypes.byref(out), None)
     assert rc == status
     assert re.search(pattern, _lib.last_error(lib))
 
 
 def test_null_pointers_are_rejected_before_launch():
     lib = _lib.load_library()
-    rc = lib.adb_decode(None, None, None, None, None, 1, 32, 8, 129, 64, None, 0, 0, None)
+    rc = lib.adb_decode(None, None, None, None, None, 1, 32, 8, 129, 64, None, 0, 0, 0, None)
     assert rc == _lib.ADB_ERR_INVALID_ARGUMENT
     assert "non-null" in _lib.last_error(lib)
     rc = lib.adb_combine(None, 0, None, 0, 1, 1, 64, None, 0, None)
