@@ -57,6 +57,10 @@ PROTOTYPES = {
         _int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _size, _uint, _int, _vp],
     ),
+    "adb_decode_no_alloc": (
+        _int,
+        [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _int, _vp],
+    ),
     "adb_combine": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
     "adb_read_error_flag": (_int, [_int, ctypes.POINTER(_int), _int]),
     "adb_launch_count": (_int, [ctypes.POINTER(_i64)]),

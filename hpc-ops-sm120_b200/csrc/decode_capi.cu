@@ -258,7 +258,8 @@ int choose_variant(const Shape& s, bool tma) {
   return s.D == 128 ? kDefaultTma128 : kDefaultTma64;
 }
 
-int make_plan(const Shape& s, bool varlen, bool tma, DeviceState* st, Plan* plan) {
+int make_plan(const Shape& s, bool varlen, bool tma, DeviceState* st, Plan* plan,
+              bool allow_steal = true) {
   int vi = choose_variant(s, tma);
   // Small problems: prefer the 64-token tile so more SMs get work.
   if (tma && forced_variant() < 0) {
@@ -274,7 +275,7 @@ int make_plan(const Shape& s, bool varlen, bool tma, DeviceState* st, Plan* plan
   if (nc < 1) nc = 1;
   plan->variant = vi;
   plan->num_ctas = nc;
-  plan->dyn_slots = v.tma ? adb::dynamic_slot_capacity(nc) : 0;
+  plan->dyn_slots = (v.tma && allow_steal) ? adb::dynamic_slot_capacity(nc) : 0;
   const size_t slots = static_cast<size_t>(nc + s.P + plan->dyn_slots);
   plan->off_claims = 0;
   plan->off_counters = static_cast<size_t>(nc) * 8;
@@ -308,7 +309,7 @@ bool is_aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t
 int run_decode(const void* q, const void* k, const void* v, const int32_t* seqlens, void* out,
                float* state_acc, float* state_ml, int64_t batch, int64_t q_heads, int64_t kv_heads,
                int64_t kv_len, int64_t head_dim, void* workspace, size_t workspace_bytes,
-               unsigned flags, int device, void* stream_ptr) {
+               unsigned flags, int device, void* stream_ptr, bool allow_steal = true) {
   Shape s;
   int rc = check_shape(batch, q_heads, kv_heads, kv_len, head_dim, &s);
   if (rc != ADB_OK) return rc;
@@ -325,7 +326,7 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
   if (rc != ADB_OK) return rc;
   const bool tma = is_aligned(k, 16) && is_aligned(v, 16);
   Plan plan;
-  rc = make_plan(s, seqlens != nullptr, tma, st, &plan);
+  rc = make_plan(s, seqlens != nullptr, tma, st, &plan, allow_steal);
   if (rc != ADB_OK) return rc;
   if (workspace == nullptr || !is_aligned(workspace, 256))
     return fail(ADB_ERR_WORKSPACE, "workspace must be a non-null 256-byte aligned device buffer");
@@ -373,7 +374,7 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
       s.P * ((s.S + var.tile_tokens - 1) / var.tile_tokens) / plan.num_ctas;
   p.max_steals = forced_steals >= 0 ? forced_steals : (tiles_per_cta >= 192 ? adb::kMaxSteals : 0);
   p.claim_divisor = claim_divisor >= 2 ? claim_divisor : 2;
-  p.steal = (var.tma && !deterministic_mode() && p.max_steals > 0) ? 1 : 0;
+  p.steal = (allow_steal && var.tma && !deterministic_mode() && p.max_steals > 0) ? 1 : 0;
   p.dyn_capacity = plan.dyn_slots;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(s.D)));
 
@@ -411,6 +412,32 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
     if (e != cudaSuccess) return cuda_fail(e, "timing event");
     t_timing.events.emplace_back(ev_start, ev_stop);
   }
+  return ADB_OK;
+}
+
+// ------------------------------------------------------------ fixed workspace
+// Scratch for adb_decode_no_alloc: one array in the module's global memory,
+// so that decoding needs no device allocation at all.  Every GPU that loads
+// the library holds ADB_NO_ALLOC_WORKSPACE_BYTES of it until the process
+// exits.  Host code cannot use the array's name as a device address; its
+// address on each device comes from cudaGetSymbolAddress (below).
+static __device__ __align__(256) unsigned char g_adb_fixed_workspace[ADB_NO_ALLOC_WORKSPACE_BYTES];
+
+std::mutex g_fixed_mutex;
+void* g_fixed_address[kMaxDevices] = {};
+
+// Device address of g_adb_fixed_workspace on `device`, which must be the
+// current device; looked up on the first call per device and kept.
+int fixed_workspace(int device, void** address) {
+  std::lock_guard<std::mutex> lock(g_fixed_mutex);
+  if (g_fixed_address[device] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_adb_fixed_workspace);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(fixed workspace)");
+    if (ptr == nullptr) return fail(ADB_ERR_CUDA, "fixed workspace has no device address");
+    g_fixed_address[device] = ptr;
+  }
+  *address = g_fixed_address[device];
   return ADB_OK;
 }
 
@@ -464,6 +491,39 @@ int adb_decode_partial(const void* q, const void* k, const void* v, const int32_
     return fail(ADB_ERR_INVALID_ARGUMENT, "partial-state pointers must be non-null");
   return run_decode(q, k, v, seqlens, nullptr, acc, ml, batch, q_heads, kv_heads, kv_len, head_dim,
                     workspace, workspace_bytes, flags, device, stream);
+}
+
+int adb_decode_no_alloc(const void* q, const void* k, const void* v, const int32_t* seqlens,
+                        void* out, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                        int64_t kv_len, int64_t head_dim, int device, void* stream) {
+  Shape s;
+  int rc = check_shape(batch, q_heads, kv_heads, kv_len, head_dim, &s);
+  if (rc != ADB_OK) return rc;
+  if (device < 0 || device >= kMaxDevices)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "device index %d out of range", device);
+  DeviceGuard guard(device);
+  if (guard.error != cudaSuccess) return cuda_fail(guard.error, "cudaSetDevice");
+  DeviceState* st = nullptr;
+  rc = probe_device(device, &st);
+  if (rc != ADB_OK) return rc;
+  // Size the scratch exactly as the launch will (no work stealing here, so
+  // no thief slots), and refuse problems that do not fit.
+  const bool tma = is_aligned(k, 16) && is_aligned(v, 16);
+  Plan plan;
+  rc = make_plan(s, seqlens != nullptr, tma, st, &plan, false);
+  if (rc != ADB_OK) return rc;
+  if (plan.bytes > ADB_NO_ALLOC_WORKSPACE_BYTES)
+    return fail(ADB_ERR_WORKSPACE,
+                "problem needs %zu bytes of scratch; the fixed workspace of adb_decode_no_alloc "
+                "holds %zu bytes (use adb_decode with a caller-provided workspace)",
+                plan.bytes, static_cast<size_t>(ADB_NO_ALLOC_WORKSPACE_BYTES));
+  void* ws = nullptr;
+  rc = fixed_workspace(device, &ws);
+  if (rc != ADB_OK) return rc;
+  // flags = 0: the scheduler header of the shared array is zeroed with one
+  // cudaMemsetAsync on `stream` before the kernel.
+  return run_decode(q, k, v, seqlens, out, nullptr, nullptr, batch, q_heads, kv_heads, kv_len,
+                    head_dim, ws, ADB_NO_ALLOC_WORKSPACE_BYTES, 0u, device, stream, false);
 }
 
 int adb_combine(const float* acc, int64_t acc_part_stride, const float* ml, int64_t ml_part_stride,

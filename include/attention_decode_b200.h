@@ -102,6 +102,39 @@ ADB_API int adb_decode(const void* q, const void* k, const void* v, const int32_
                        int64_t kv_len, int64_t head_dim, void* workspace,
                        size_t workspace_bytes, unsigned flags, int device, void* stream);
 
+/* Size of the fixed device array that adb_decode_no_alloc uses as its
+ * workspace (8 MiB, held by every GPU that loads the library). */
+#define ADB_NO_ALLOC_WORKSPACE_BYTES (8u << 20)
+
+/* Decode exactly like adb_decode, but without any workspace argument and
+ * without allocating device memory: the scratch is a fixed array of
+ * ADB_NO_ALLOC_WORKSPACE_BYTES inside the library.  It has no counterpart in
+ * the reference, whose entry point always allocates its partial buffer.
+ *
+ * It is meant for callers that cannot allocate device memory themselves:
+ * hosts binding the C ABI from another language whose device memory is owned
+ * by a different allocator, and serving loops that must not enter
+ * cudaMalloc/cudaFree (which synchronise the device) or run under a fixed
+ * memory budget.  The caller still passes Q, K, V, seqlens and the output.
+ *
+ * Limits and behaviour:
+ *  - problems whose scratch would exceed ADB_NO_ALLOC_WORKSPACE_BYTES are
+ *    rejected with ADB_ERR_WORKSPACE (roughly (148 + batch*kv_heads) *
+ *    group * head_dim * 4 bytes must fit; no work stealing is used here);
+ *  - the first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture;
+ *  - every call uses the same array, and its scheduler header is cleared with
+ *    one cudaMemsetAsync on `stream` before the kernel, so calls that overlap
+ *    on the GPU (different streams, or different host threads) race and
+ *    corrupt each other's results: order them on one stream or use
+ *    adb_decode;
+ *  - no cudaMalloc, cudaFree or other allocating call is made. */
+ADB_API int adb_decode_no_alloc(const void* q, const void* k, const void* v,
+                                const int32_t* seqlens, void* out, int64_t batch,
+                                int64_t q_heads, int64_t kv_heads, int64_t kv_len,
+                                int64_t head_dim, int device, void* stream);
+
 /* Partial decode for sequence sharding: instead of the normalised output it
  * writes, per query-head row r = b * q_heads + hq,
  *   acc[r, 0:head_dim]  unnormalised sum_t exp(s_t - m) * V_t   (fp32)
