@@ -49,46 +49,48 @@ def _fail(message: str):
 def _validate(q, k, v, seqlens=None):
     """Mirror of the reference's checks (attention_decode/__init__.py:35-38
     and csrc/decode.cu:225-241), with the INT_MAX size limit dropped (64-bit
-    indexing) and G = 8 accepted."""
+    indexing) and G = 8 accepted.  Written as straight-line checks: this runs
+    on every decode call."""
     torch = _torch()
-    if not all(isinstance(x, torch.Tensor) for x in (q, k, v)):
+    Tensor = torch.Tensor
+    if not (isinstance(q, Tensor) and isinstance(k, Tensor) and isinstance(v, Tensor)):
         raise TypeError("Q, K, and V must be tensors")
-    if not all(x.is_cuda for x in (q, k, v)):
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
         raise ValueError("Q, K, and V must be CUDA tensors")
-    for x in (q, k, v):
-        if x.dtype != torch.bfloat16:
-            _fail("Q/K/V dtype must be BF16 (bfloat16)")
-        if x.dim() != 4:
-            _fail("Q/K/V must have rank four")
-        if not x.is_contiguous():
-            _fail("Q/K/V must be contiguous")
-        if x.requires_grad:
-            _fail("attention_decode is forward inference only; no backward/grad support")
-        if x.numel() == 0:
-            _fail("empty tensors are unsupported")
+    bf16 = torch.bfloat16
+    if q.dtype is not bf16 or k.dtype is not bf16 or v.dtype is not bf16:
+        _fail("Q/K/V dtype must be BF16 (bfloat16)")
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        _fail("Q/K/V must have rank four")
+    if not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
+        _fail("Q/K/V must be contiguous")
+    if q.requires_grad or k.requires_grad or v.requires_grad:
+        _fail("attention_decode is forward inference only; no backward/grad support")
+    if q.numel() == 0 or k.numel() == 0 or v.numel() == 0:
+        _fail("empty tensors are unsupported")
     if q.device != k.device or q.device != v.device:
         _fail("Q/K/V device must match")
-    if k.shape != v.shape:
+    qs, ks = q.shape, k.shape
+    if ks != v.shape:
         _fail("K/V shape must match")
-    if q.shape[2] != 1:
+    if qs[2] != 1:
         _fail("query length must be 1")
-    if q.shape[0] != k.shape[0] or q.shape[3] != k.shape[3]:
+    if qs[0] != ks[0] or qs[3] != ks[3]:
         _fail("Q/K/V batch and head dimension must match")
-    if q.shape[1] % k.shape[1] != 0:
+    if qs[1] % ks[1] != 0:
         _fail("query heads must be divisible by KV heads")
-    group = q.shape[1] // k.shape[1]
-    if group not in _GROUPS:
+    if qs[1] // ks[1] not in _GROUPS:
         _fail("supported GQA group sizes are 1, 4 and 8")
-    if q.shape[3] not in _DIMS:
+    if qs[3] not in _DIMS:
         _fail("head dimension must be 64 or 128")
     if seqlens is not None:
-        if not isinstance(seqlens, torch.Tensor):
+        if not isinstance(seqlens, Tensor):
             raise TypeError("seqlens must be a tensor")
         if seqlens.device != q.device:
             _fail("seqlens must be on the same CUDA device as Q/K/V")
         if seqlens.dtype != torch.int32:
             _fail("seqlens dtype must be int32")
-        if seqlens.dim() != 1 or seqlens.shape[0] != q.shape[0] or not seqlens.is_contiguous():
+        if seqlens.dim() != 1 or seqlens.shape[0] != qs[0] or not seqlens.is_contiguous():
             _fail("seqlens must be a contiguous [batch] tensor")
 
 
@@ -134,7 +136,7 @@ class _StreamWorkspace:
 def _workspace(device_obj, device: int, stream: int, nbytes: int, header: int):
     torch = _torch()
     nbytes = max(nbytes, 256)
-    if torch.cuda.is_current_stream_capturing():
+    if torch._C._cuda_isCurrentStreamCapturing():
         # A captured call owns its buffer in the graph's pool; the library's
         # header memset is captured with it.
         return torch.empty(nbytes, dtype=torch.uint8, device=device_obj), 0
@@ -158,7 +160,7 @@ def _launch(q, k, v, seqlens, out=None, acc=None, ml=None):
     kv_heads, kv_len = k.shape[1], k.shape[2]
     device = q.device.index if q.device.index is not None else torch.cuda.current_device()
     nbytes, header = workspace_bytes(batch, q_heads, kv_heads, kv_len, head_dim, seqlens is not None, device)
-    stream = torch.cuda.current_stream(q.device).cuda_stream
+    stream = torch._C._cuda_getCurrentRawStream(device)
     workspace, flags = _workspace(q.device, device, stream, nbytes, header)
     lens = seqlens.data_ptr() if seqlens is not None else None
     if out is not None:
@@ -186,7 +188,7 @@ def attention_decode(q, k, v, seqlens=None):
     stream.
     """
     _validate(q, k, v, seqlens)
-    out = _torch().empty(q.shape, dtype=q.dtype, device=q.device)
+    out = _torch().empty_like(q)
     _launch(q, k, v, seqlens, out=out)
     return out
 

@@ -206,6 +206,40 @@ int encode_kv_map(CUtensorMap* map, const void* base, int64_t pairs, int64_t S, 
   return ADB_OK;
 }
 
+// Encoded descriptors of the last few K/V tensors this thread used: a decode
+// loop passes the same cache buffers every step, and re-encoding costs host
+// time on every call.
+struct MapCacheEntry {
+  const void* base = nullptr;
+  int64_t pairs = 0, S = 0, D = 0;
+  int tile_tokens = 0;
+  CUtensorMap map;
+};
+constexpr int kMapCacheEntries = 8;
+thread_local MapCacheEntry t_map_cache[kMapCacheEntries];
+thread_local int t_map_cache_next = 0;
+
+int kv_map(CUtensorMap* map, const void* base, int64_t pairs, int64_t S, int64_t D,
+           int tile_tokens) {
+  for (const MapCacheEntry& e : t_map_cache)
+    if (e.base == base && e.pairs == pairs && e.S == S && e.D == D &&
+        e.tile_tokens == tile_tokens) {
+      *map = e.map;
+      return ADB_OK;
+    }
+  const int rc = encode_kv_map(map, base, pairs, S, D, tile_tokens);
+  if (rc != ADB_OK) return rc;
+  MapCacheEntry& e = t_map_cache[t_map_cache_next];
+  t_map_cache_next = (t_map_cache_next + 1) % kMapCacheEntries;
+  e.base = base;
+  e.pairs = pairs;
+  e.S = S;
+  e.D = D;
+  e.tile_tokens = tile_tokens;
+  e.map = *map;
+  return ADB_OK;
+}
+
 // ------------------------------------------------------------ plan
 struct Shape {
   int64_t B, Hq, Hkv, S, D, G, P;
@@ -339,9 +373,9 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
   std::memset(&tm_k, 0, sizeof(tm_k));
   std::memset(&tm_v, 0, sizeof(tm_v));
   if (var.tma) {
-    rc = encode_kv_map(&tm_k, k, s.P, s.S, s.D, var.tile_tokens);
+    rc = kv_map(&tm_k, k, s.P, s.S, s.D, var.tile_tokens);
     if (rc != ADB_OK) return rc;
-    rc = encode_kv_map(&tm_v, v, s.P, s.S, s.D, var.tile_tokens);
+    rc = kv_map(&tm_v, v, s.P, s.S, s.D, var.tile_tokens);
     if (rc != ADB_OK) return rc;
   }
 
