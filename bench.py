@@ -12,8 +12,10 @@ Metric: achieved HBM GB/s = algorithmic bytes per step (valid K+V, Q read,
 O write) / step time, summed over ranks; us/step is reported beside it.
 Multi-GPU (torchrun, one process per GPU, NCCL): cfg1/2/3/5 are batch-sharded
 with no collective (each rank runs its own full copy of the workload: weak
-scaling); cfg4 is sequence-sharded (each rank holds S/N tokens, partial
-states are all-gathered over NVLink and merged: strong scaling).
+scaling); cfg4 is sequence-sharded (each rank holds S/N tokens; the decode
+kernel stores its partial states into every rank's exchange buffer over
+NVLink and a merge kernel combines them on each rank, or with
+`--transport nccl` the states are all-gathered over NCCL: strong scaling).
 
 `--impl reference` times the reference's FP32 algorithm on the host cores
 (the numpy oracle restating attention_decode/reference.py:47-60) on a bounded
@@ -51,6 +53,8 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--config", default="cfg2", choices=("cfg1", "cfg2", "cfg3", "cfg4", "cfg5"))
     p.add_argument("--impl", default="b200", choices=("b200", "reference"))
+    p.add_argument("--transport", default="p2p", choices=("p2p", "nccl"),
+                   help="cfg4 at N>1: state exchange through NVLink peer memory (p2p) or an NCCL all_gather")
     p.add_argument("--seed", type=int, default=2026)
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle timing")
     p.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end pass (default: --steps, at most 500)")
@@ -291,11 +295,15 @@ def run_gpu_arm(args):
         k = k[:, :, lo:hi].contiguous()
         v = v[:, :, lo:hi].contiguous()
         torch.cuda.empty_cache()
-        step_fn = sharded.SequenceShardedDecode(q, k, v, group=None)
+        step_fn = sharded.SequenceShardedDecode(q, k, v, group=None, transport=args.transport)
         bytes_per_rank = 2 * 2 * cfg.head_dim * cfg.kv_heads * cfg.batch * (hi - lo) + (2 * 2 * cfg.batch * cfg.query_heads * cfg.head_dim if rank == 0 else 0)
         step = step_fn
         scaling = "strong"
-        parallelism = f"sequence-shard sp{world} (all_gather of partial states over NCCL)"
+        parallelism = (
+            f"sequence-shard sp{world} (partial states stored to every rank over NVLink by the decode kernel, merged on each rank)"
+            if args.transport == "p2p"
+            else f"sequence-shard sp{world} (all_gather of partial states over NCCL)"
+        )
     else:
         bytes_per_rank = cfg.algorithmic_bytes(seqlens)
 
@@ -350,6 +358,9 @@ def run_gpu_arm(args):
     launches_timed = ctypes_count(lib) - launches_before
     barrier(world)
     clocks = sampler.stop()
+    error_word = ad.read_error_flag(local_rank)
+    if error_word:
+        raise SystemExit(f"bench: a kernel reported device error word {error_word} (bounded wait expired)")
     ms_step = start.elapsed_time(stop) / args.steps
     ms_step = max_over_ranks(ms_step, world, device)
     total_bytes = bytes_per_rank * (world if not sequence_sharded else 1)
@@ -370,7 +381,7 @@ def run_gpu_arm(args):
     isolated_ms = tot_ms.value / max(n_launch.value, 1)
     isolated_ms = max_over_ranks(isolated_ms, world, device)
     # Every step is exactly one decode_stream_kernel launch (plus, when
-    # sequence-sharded, the NCCL gather and the small merge), so the kernel's
+    # sequence-sharded, the state exchange and the small merge), so the kernel's
     # average duration in the timed region is the timed region over its
     # launches.  Event pairs around single launches (isolated_ms) also time
     # the launch latency that back-to-back launches hide.

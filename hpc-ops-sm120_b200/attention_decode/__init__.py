@@ -178,6 +178,28 @@ def _launch(q, k, v, seqlens, out=None, acc=None, ml=None):
     _lib.check(lib, status)
 
 
+def _launch_exchange(q, k, v, seqlens, bases, rank: int):
+    """adb_decode_exchange: partial decode whose states go to slot `rank` of
+    every exchange buffer in `bases` (device addresses as mapped here)."""
+    torch = _torch()
+    lib = _lib.load_library()
+    batch, q_heads, _, head_dim = q.shape
+    kv_heads, kv_len = k.shape[1], k.shape[2]
+    device = q.device.index if q.device.index is not None else torch.cuda.current_device()
+    nbytes, header = workspace_bytes(batch, q_heads, kv_heads, kv_len, head_dim, seqlens is not None, device)
+    stream = torch._C._cuda_getCurrentRawStream(device)
+    workspace, flags = _workspace(q.device, device, stream, nbytes, header)
+    lens = seqlens.data_ptr() if seqlens is not None else None
+    array = (ctypes.c_void_p * len(bases))(*bases)
+    _lib.check(
+        lib,
+        lib.adb_decode_exchange(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), lens, batch, q_heads, kv_heads, kv_len, head_dim,
+            array, len(bases), rank, workspace.data_ptr(), workspace.numel(), flags, device, stream,
+        ),
+    )
+
+
 def attention_decode(q, k, v, seqlens=None):
     """Forward-only single-query attention for contiguous BF16 CUDA tensors.
 

@@ -25,6 +25,8 @@ ADB_ERR_DEVICE = 3
 ADB_ERR_WORKSPACE = 4
 ADB_ERR_CUDA = 5
 ADB_FLAG_HEADER_ZEROED = 1
+ADB_IPC_HANDLE_BYTES = 64
+ADB_ERROR_FLAG_PEER_TIMEOUT = 4
 
 STATUS_NAMES = {
     ADB_OK: "ok",
@@ -62,6 +64,18 @@ PROTOTYPES = {
         [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _int, _vp],
     ),
     "adb_combine": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
+    "adb_exchange_size": (_int, [_i64, _i64, _int, ctypes.POINTER(ctypes.c_size_t)]),
+    "adb_exchange_alloc": (_int, [ctypes.c_size_t, _int, ctypes.POINTER(_vp)]),
+    "adb_exchange_free": (_int, [_vp, _int]),
+    "adb_ipc_handle": (_int, [_vp, _int, ctypes.c_char_p]),
+    "adb_ipc_open": (_int, [ctypes.c_char_p, _int, ctypes.POINTER(_vp)]),
+    "adb_ipc_close": (_int, [_vp, _int]),
+    "adb_decode_exchange": (
+        _int,
+        [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_vp), _int, _int,
+         _vp, ctypes.c_size_t, ctypes.c_uint, _int, _vp],
+    ),
+    "adb_exchange_merge": (_int, [_vp, _int, _i64, _i64, _vp, _i64, _int, _vp]),
     "adb_read_error_flag": (_int, [_int, ctypes.POINTER(_int), _int]),
     "adb_launch_count": (_int, [ctypes.POINTER(_i64)]),
     "adb_timing_enable": (_int, [_int]),

@@ -9,11 +9,17 @@ same kernels here:
   ``balance_by_tokens`` partitions variable-length sequences so every rank
   streams about the same number of KV bytes (greedy longest-first).
 * Sequence sharding (very long contexts): rank r owns tokens
-  ``token_shard(S, r, R)`` of every sequence.  Each rank computes its partial
-  state (acc, m, l) per query head with ``attention_decode_partial``; the
-  packed states (33,280 B per rank at Hq=64, D=128) are all-gathered over
-  NCCL and merged by the same LSE combine kernel (``combine_partials``) on
-  every rank, so the output is replicated.
+  ``token_shard(S, r, R)`` of every sequence and computes its partial state
+  (acc, m, l) per query head; the states (33,280 B per rank at Hq=64,
+  D=128) of all ranks are merged on every rank, so the output is
+  replicated.  Two transports:
+
+  - ``"p2p"`` (default): the decode kernel itself stores its states into
+    every rank's exchange buffer over NVLink (peer memory mapped with CUDA
+    IPC) and raises a flag there; a small merge kernel waits for the flags
+    and merges.  Two launches per step, no collective library call.
+  - ``"nccl"``: ``attention_decode_partial``, an NCCL all_gather of the
+    packed states, then ``combine_partials``.
 
 The state packing and merge order are plain host logic and are covered on
 CPU by gloo-rank tests.
@@ -21,11 +27,14 @@ CPU by gloo-rank tests.
 
 from __future__ import annotations
 
+import ctypes
 import heapq
 
 import torch
 
-from . import attention_decode_partial, combine_partials
+from . import _launch_exchange, _lib, attention_decode_partial, combine_partials
+
+DEFAULT_PEER_TIMEOUT_S = 2.0
 
 
 def token_shard(length: int, rank: int, world: int) -> tuple[int, int]:
@@ -67,6 +76,96 @@ def unpack_gathered(gathered: torch.Tensor, world: int, rows: int, head_dim: int
     return g[:, :ml_off].view(world, rows, head_dim), g[:, ml_off:].view(world, rows, 2)
 
 
+class PeerExchange:
+    """Exchange buffers of a sequence-sharded decode over NVLink peer memory.
+
+    Collective: every rank of `group` constructs it with the same `rows`
+    (= batch * q_heads) and `head_dim`.  Each rank allocates one zeroed
+    buffer in its own HBM (adb_exchange_alloc), the CUDA IPC handles are
+    all-gathered over `group`, and each rank maps the other ranks' buffers;
+    ``bases[r]`` is rank r's buffer as seen from this process.  ``close``
+    (also collective) unmaps and frees after every rank's work is done."""
+
+    def __init__(self, rows: int, head_dim: int, group=None, device=None, *, _world=None):
+        self.lib = _lib.load_library()
+        self.rows, self.head_dim = int(rows), int(head_dim)
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.index = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        self.group = group
+        self._own: list[int] = []
+        self._mapped: list[int] = []
+        if _world is not None:  # single-process emulation (see `emulated`)
+            self.dist, self.world, self.rank = None, _world, None
+            self.bases = [self._alloc() for _ in range(_world)]
+            return
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        mine = self._alloc()
+        handle = ctypes.create_string_buffer(_lib.ADB_IPC_HANDLE_BYTES)
+        _lib.check(self.lib, self.lib.adb_ipc_handle(mine, self.index, handle))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self.bases = []
+        for r, raw in enumerate(handles):
+            if r == self.rank:
+                self.bases.append(mine)
+                continue
+            ptr = ctypes.c_void_p()
+            _lib.check(self.lib, self.lib.adb_ipc_open(raw, self.index, ctypes.byref(ptr)))
+            self._mapped.append(ptr.value)
+            self.bases.append(ptr.value)
+        dist.barrier(group=group)
+
+    @classmethod
+    def emulated(cls, world: int, rows: int, head_dim: int, device=None) -> "PeerExchange":
+        """`world` buffers on one GPU in one process, for driving the ranks'
+        steps one after another (tests of the data path and the flags)."""
+        return cls(rows, head_dim, device=device, _world=world)
+
+    def _alloc(self) -> int:
+        size = ctypes.c_size_t(0)
+        _lib.check(self.lib, self.lib.adb_exchange_size(self.rows, self.head_dim, self.world, ctypes.byref(size)))
+        ptr = ctypes.c_void_p()
+        _lib.check(self.lib, self.lib.adb_exchange_alloc(size.value, self.index, ctypes.byref(ptr)))
+        self._own.append(ptr.value)
+        return ptr.value
+
+    def decode(self, q, k, v, rank: int | None = None, seqlens=None):
+        """This rank's partial decode; its states go to every rank's buffer."""
+        _launch_exchange(q, k, v, seqlens, self.bases, self.rank if rank is None else rank)
+
+    def merge(self, out, rank: int | None = None, timeout_s: float = DEFAULT_PEER_TIMEOUT_S):
+        """Wait for every rank's states of this call (bounded) and merge them
+        into `out` (contiguous BF16, rows * head_dim elements)."""
+        if out.dtype != torch.bfloat16 or not out.is_contiguous() or out.numel() != self.rows * self.head_dim:
+            raise ValueError("out must be a contiguous bf16 buffer of rows * head_dim elements")
+        r = self.rank if rank is None else rank
+        stream = torch._C._cuda_getCurrentRawStream(self.index)
+        _lib.check(
+            self.lib,
+            self.lib.adb_exchange_merge(
+                self.bases[r], self.world, self.rows, self.head_dim, out.data_ptr(),
+                max(1, int(timeout_s * 1e6)), self.index, stream,
+            ),
+        )
+        return out
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (collective)."""
+        if self.bases is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.dist is not None:
+            self.dist.barrier(group=self.group)
+        for ptr in self._mapped:
+            _lib.check(self.lib, self.lib.adb_ipc_close(ptr, self.index))
+        for ptr in self._own:
+            _lib.check(self.lib, self.lib.adb_exchange_free(ptr, self.index))
+        self._mapped, self._own, self.bases = [], [], None
+
+
 class SequenceShardedDecode:
     """Callable decode step over a sequence-sharded KV cache.
 
@@ -79,23 +178,33 @@ class SequenceShardedDecode:
     step's merge, which graph replays serialise); the graph helps when the
     host is the bottleneck."""
 
-    def __init__(self, q, k_local, v_local, group=None, seqlens_local=None):
+    def __init__(self, q, k_local, v_local, group=None, seqlens_local=None, transport: str = "p2p",
+                 timeout_s: float = DEFAULT_PEER_TIMEOUT_S):
         import torch.distributed as dist
 
+        if transport not in ("p2p", "nccl"):
+            raise ValueError(f"unknown transport {transport!r} (expected 'p2p' or 'nccl')")
         self.dist = dist
         self.group = group
         self.world = dist.get_world_size(group)
+        self.transport = transport
+        self.timeout_s = timeout_s
         self.q, self.k, self.v, self.seqlens = q, k_local, v_local, seqlens_local
         batch, q_heads, _, head_dim = q.shape
         self.shape = q.shape
         self.rows, self.head_dim = batch * q_heads, head_dim
+        self.out = torch.empty((self.rows, head_dim), dtype=torch.bfloat16, device=q.device)
+        self.graph = None
+        self.exchange = None
+        self.buf = self.gathered = None
+        if transport == "p2p":
+            self.exchange = PeerExchange(self.rows, head_dim, group, q.device)
+            return
         block, ml_off = state_layout(self.rows, head_dim)
         self.buf = torch.empty(block, dtype=torch.float32, device=q.device)
         self.acc = self.buf[:ml_off].view(batch, q_heads, head_dim)
         self.ml = self.buf[ml_off:].view(batch, q_heads, 2)
         self.gathered = torch.empty(self.world * block, dtype=torch.float32, device=q.device)
-        self.out = torch.empty((self.rows, head_dim), dtype=torch.bfloat16, device=q.device)
-        self.graph = None
 
     def capture(self, warmup: int = 3):
         """Record one step (partial decode, all_gather, merge) reading
@@ -113,6 +222,10 @@ class SequenceShardedDecode:
         return self
 
     def run(self, q):
+        if self.exchange is not None:
+            self.exchange.decode(q, self.k, self.v, seqlens=self.seqlens)
+            self.exchange.merge(self.out, timeout_s=self.timeout_s)
+            return self.out.view(self.shape)
         attention_decode_partial(q, self.k, self.v, self.seqlens, out_acc=self.acc, out_ml=self.ml)
         self.dist.all_gather_into_tensor(self.gathered, self.buf, group=self.group)
         acc, ml = unpack_gathered(self.gathered, self.world, self.rows, self.head_dim)
@@ -139,11 +252,20 @@ class SequenceShardedDecode:
         return step
 
     def release(self):
-        """Drop the graph and the buffers (call before destroy_process_group)."""
+        """Drop the graph and the buffers (collective; call on every rank
+        before destroy_process_group)."""
         self.graph = None
+        if self.exchange is not None:
+            self.exchange.close()
+            self.exchange = None
         self.buf = self.gathered = self.out = None
 
 
-def attention_decode_sequence_sharded(q, k_local, v_local, group=None, seqlens_local=None):
-    """One sequence-sharded decode (allocates its buffers; see SequenceShardedDecode)."""
-    return SequenceShardedDecode(q, k_local, v_local, group, seqlens_local)()
+def attention_decode_sequence_sharded(q, k_local, v_local, group=None, seqlens_local=None, transport="p2p"):
+    """One sequence-sharded decode (sets up and releases its buffers; see
+    SequenceShardedDecode).  Returns a new output tensor."""
+    step = SequenceShardedDecode(q, k_local, v_local, group, seqlens_local, transport=transport)
+    try:
+        return step().clone()
+    finally:
+        step.release()

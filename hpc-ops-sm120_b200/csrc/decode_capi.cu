@@ -57,14 +57,21 @@ struct Variant {
   int threads;
   int smem_bytes;
   bool tma;
-  const void* fn;
+  const void* fn;     // ordinary decode / partial decode
+  const void* fn_x;   // partial decode into peer exchange buffers
 };
 
 template <int D, int W, int MB, int ST, bool TMA>
 constexpr Variant make_variant(const char* name) {
   using C = adb::StreamCfg<D, W, MB, ST, TMA>;
-  return Variant{name,     D,   C::kTT, C::kThreads, C::kSmemBytes,
-                 TMA,      reinterpret_cast<const void*>(&adb::decode_stream_kernel<D, W, MB, ST, TMA>)};
+  return Variant{name,
+                 D,
+                 C::kTT,
+                 C::kThreads,
+                 C::kSmemBytes,
+                 TMA,
+                 reinterpret_cast<const void*>(&adb::decode_stream_kernel<D, W, MB, ST, TMA, false>),
+                 reinterpret_cast<const void*>(&adb::decode_stream_kernel<D, W, MB, ST, TMA, true>)};
 }
 
 // Name format: d<head_dim>_<tma|generic>_tt<tile tokens>_s<stages>.
@@ -154,6 +161,8 @@ int prepare_variant(DeviceState* st, int vi) {
   const Variant& v = kVariants[vi];
   cudaError_t e =
       cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem_bytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(v.fn_x, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem_bytes);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
   int blocks = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, v.fn, v.threads, v.smem_bytes);
@@ -340,18 +349,27 @@ struct DeviceGuard {
 
 bool is_aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
+// Destinations of a decode whose partial states go to every rank's exchange
+// buffer (adb_decode_exchange).
+struct ExchangeArgs {
+  uint8_t* base[adb::kMaxRanks];
+  int world;
+  int rank;
+};
+
 int run_decode(const void* q, const void* k, const void* v, const int32_t* seqlens, void* out,
                float* state_acc, float* state_ml, int64_t batch, int64_t q_heads, int64_t kv_heads,
                int64_t kv_len, int64_t head_dim, void* workspace, size_t workspace_bytes,
-               unsigned flags, int device, void* stream_ptr, bool allow_steal = true) {
+               unsigned flags, int device, void* stream_ptr, bool allow_steal = true,
+               const ExchangeArgs* exchange = nullptr) {
   Shape s;
   int rc = check_shape(batch, q_heads, kv_heads, kv_len, head_dim, &s);
   if (rc != ADB_OK) return rc;
-  const bool partial = state_acc != nullptr;
+  const bool partial = state_acc != nullptr || exchange != nullptr;
   if (q == nullptr || k == nullptr || v == nullptr)
     return fail(ADB_ERR_INVALID_ARGUMENT, "Q, K and V pointers must be non-null");
   if (!partial && out == nullptr) return fail(ADB_ERR_INVALID_ARGUMENT, "output pointer is null");
-  if (partial && state_ml == nullptr)
+  if (partial && exchange == nullptr && state_ml == nullptr)
     return fail(ADB_ERR_INVALID_ARGUMENT, "partial-state pointers must be non-null");
   DeviceGuard guard(device);
   if (guard.error != cudaSuccess) return cuda_fail(guard.error, "cudaSetDevice");
@@ -411,6 +429,14 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
   p.steal = (allow_steal && var.tma && !deterministic_mode() && p.max_steals > 0) ? 1 : 0;
   p.dyn_capacity = plan.dyn_slots;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(s.D)));
+  for (int r = 0; r < adb::kMaxRanks; ++r) p.x_base[r] = nullptr;
+  p.x_world = 0;
+  p.x_rank = 0;
+  if (exchange != nullptr) {
+    for (int r = 0; r < exchange->world; ++r) p.x_base[r] = exchange->base[r];
+    p.x_world = exchange->world;
+    p.x_rank = exchange->rank;
+  }
 
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   if (!(flags & ADB_FLAG_HEADER_ZEROED)) {
@@ -438,7 +464,7 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   void* args[] = {&tm_k, &tm_v, &p};
-  cudaError_t e = cudaLaunchKernelExC(&cfg, var.fn, args);
+  cudaError_t e = cudaLaunchKernelExC(&cfg, exchange != nullptr ? var.fn_x : var.fn, args);
   if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   if (t_timing.enabled) {
@@ -591,6 +617,144 @@ int adb_combine(const float* acc, int64_t acc_part_stride, const float* ml, int6
                                                            ml_part_stride, parts, rows, o);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return ADB_OK;
+}
+
+int adb_exchange_size(int64_t rows, int64_t head_dim, int world, size_t* bytes) {
+  if (bytes == nullptr) return fail(ADB_ERR_INVALID_ARGUMENT, "bytes pointer is null");
+  if (rows <= 0) return fail(ADB_ERR_INVALID_ARGUMENT, "rows must be positive");
+  if (world < 1 || world > adb::kMaxRanks)
+    return fail(ADB_ERR_UNSUPPORTED, "world size must be 1..%d (got %d)", adb::kMaxRanks, world);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(ADB_ERR_UNSUPPORTED, "head dimension must be 64 or 128 (got %lld)",
+                (long long)head_dim);
+  *bytes = adb::x_bytes(world, rows, static_cast<int>(head_dim));
+  return ADB_OK;
+}
+
+int adb_exchange_alloc(size_t bytes, int device, void** buffer) {
+  if (buffer == nullptr || bytes == 0)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "buffer pointer is null or size is zero");
+  *buffer = nullptr;
+  DeviceGuard guard(device);
+  if (guard.error != cudaSuccess) return cuda_fail(guard.error, "cudaSetDevice");
+  void* ptr = nullptr;
+  cudaError_t e = cudaMalloc(&ptr, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(exchange buffer)");
+  e = cudaMemset(ptr, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(ptr);
+    return cuda_fail(e, "zeroing the exchange buffer");
+  }
+  *buffer = ptr;
+  return ADB_OK;
+}
+
+int adb_exchange_free(void* buffer, int device) {
+  if (buffer == nullptr) return ADB_OK;
+  DeviceGuard guard(device);
+  if (guard.error != cudaSuccess) return cuda_fail(guard.error, "cudaSetDevice");
+  const cudaError_t e = cudaFree(buffer);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFree(exchange buffer)");
+  return ADB_OK;
+}
+
+int adb_ipc_handle(void* buffer, int device, unsigned char* handle) {
+  if (buffer == nullptr || handle == nullptr)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "buffer and handle pointers must be non-null");
+  static_assert(sizeof(cudaIpcMemHandle_t) == ADB_IPC_HANDLE_BYTES, "IPC handle size");
+  DeviceGuard guard(device);
+  if (guard.error != cudaSuccess) return cuda_fail(guard.error, "cudaSetDevice");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, buffer);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  std::memcpy(handle, &h, sizeof(h));
+  return ADB_OK;
+}
+
+int adb_ipc_open(const unsigned char* handle, int device, void** buffer) {
+  if (buffer == nullptr || handle == nullptr)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "buffer and handle pointers must be non-null");
+  *buffer = nullptr;
+  DeviceGuard guard(device);
+  if (guard.error != cudaSuccess) return cuda_fail(guard.error, "cudaSetDevice");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(buffer, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  return ADB_OK;
+}
+
+int adb_ipc_close(void* buffer, int device) {
+  if (buffer == nullptr) return ADB_OK;
+  DeviceGuard guard(device);
+  if (guard.error != cudaSuccess) return cuda_fail(guard.error, "cudaSetDevice");
+  const cudaError_t e = cudaIpcCloseMemHandle(buffer);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return ADB_OK;
+}
+
+int adb_decode_exchange(const void* q, const void* k, const void* v, const int32_t* seqlens,
+                        int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t kv_len,
+                        int64_t head_dim, void* const* exchange, int world, int rank,
+                        void* workspace, size_t workspace_bytes, unsigned flags, int device,
+                        void* stream) {
+  if (exchange == nullptr) return fail(ADB_ERR_INVALID_ARGUMENT, "exchange array is null");
+  if (world < 1 || world > adb::kMaxRanks)
+    return fail(ADB_ERR_UNSUPPORTED, "world size must be 1..%d (got %d)", adb::kMaxRanks, world);
+  if (rank < 0 || rank >= world)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "rank %d is outside 0..%d", rank, world - 1);
+  ExchangeArgs x;
+  for (int r = 0; r < adb::kMaxRanks; ++r) x.base[r] = nullptr;
+  for (int r = 0; r < world; ++r) {
+    if (exchange[r] == nullptr || !is_aligned(exchange[r], 256))
+      return fail(ADB_ERR_INVALID_ARGUMENT, "exchange buffer of rank %d is null or misaligned", r);
+    x.base[r] = static_cast<uint8_t*>(exchange[r]);
+  }
+  x.world = world;
+  x.rank = rank;
+  return run_decode(q, k, v, seqlens, nullptr, nullptr, nullptr, batch, q_heads, kv_heads, kv_len,
+                    head_dim, workspace, workspace_bytes, flags, device, stream, true, &x);
+}
+
+int adb_exchange_merge(const void* exchange, int world, int64_t rows, int64_t head_dim, void* out,
+                       int64_t timeout_us, int device, void* stream) {
+  if (exchange == nullptr || out == nullptr)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "exchange and output pointers must be non-null");
+  if (world < 1 || world > adb::kMaxRanks)
+    return fail(ADB_ERR_UNSUPPORTED, "world size must be 1..%d (got %d)", adb::kMaxRanks, world);
+  if (rows <= 0) return fail(ADB_ERR_INVALID_ARGUMENT, "rows must be positive");
+  if (head_dim != 64 && head_dim != 128)
+    return fail(ADB_ERR_UNSUPPORTED, "head dimension must be 64 or 128 (got %lld)",
+                (long long)head_dim);
+  if (timeout_us <= 0) return fail(ADB_ERR_INVALID_ARGUMENT, "timeout must be positive");
+  DeviceGuard guard(device);
+  if (guard.error != cudaSuccess) return cuda_fail(guard.error, "cudaSetDevice");
+  DeviceState* st = nullptr;
+  int rc = probe_device(device, &st);
+  if (rc != ADB_OK) return rc;
+  const int warps = 8;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((rows + warps - 1) / warps));
+  cfg.blockDim = dim3(warps * 32);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const uint8_t* xb = static_cast<const uint8_t*>(exchange);
+  __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+  const uint64_t timeout_ns = static_cast<uint64_t>(timeout_us) * 1000ull;
+  cudaError_t e;
+  if (head_dim == 128)
+    e = cudaLaunchKernelEx(&cfg, adb::exchange_merge_kernel<128>, xb, world, rows, o, timeout_ns);
+  else
+    e = cudaLaunchKernelEx(&cfg, adb::exchange_merge_kernel<64>, xb, world, rows, o, timeout_ns);
+  if (e != cudaSuccess) return cuda_fail(e, "exchange merge kernel launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return ADB_OK;
 }

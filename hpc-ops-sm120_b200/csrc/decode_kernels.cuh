@@ -65,6 +65,32 @@ constexpr int kMaxTableBatches = 1024;  // varlen: per-batch tile table kept in 
 constexpr int kStealChunk = 4;          // most tiles one steal takes
 constexpr int kStealMinRemaining = 4;   // a victim with fewer claimable tiles is left alone
 
+// ---------------------------------------------------------------- exchange
+// Sequence sharding over NVLink peer memory.  Every rank owns one exchange
+// buffer in its own HBM, mapped into every other rank's process (CUDA IPC):
+//   [0, 64)     u32 flags[kMaxRanks]: the last call number rank s delivered
+//   [64, 68)    u32 epoch: decode calls this rank has completed
+//   [256, ...)  acc f32[2][world][rows][D]   partial states, by call parity,
+//   then        ml  f32[2][world][rows][2]   then by the sending rank
+// A rank's decode stores its states into its slot of every buffer (parity of
+// its next call number), fences at system scope, and raises its flag in
+// every buffer; the merge on each rank waits for all flags to reach the
+// call number and merges the `world` slots of that parity.  A rank can run
+// at most one call ahead of another (its next merge needs the other's
+// states), so two parities never collide.
+constexpr int kMaxRanks = 8;
+constexpr size_t kXFlagsOffset = 0;
+constexpr size_t kXEpochOffset = 64;
+constexpr size_t kXAccOffset = 256;
+
+__host__ __device__ constexpr size_t x_align256(size_t x) { return (x + 255) & ~size_t(255); }
+__host__ __device__ constexpr size_t x_ml_offset(int world, int64_t rows, int d) {
+  return kXAccOffset + x_align256(size_t(2) * world * rows * d * sizeof(float));
+}
+__host__ __device__ constexpr size_t x_bytes(int world, int64_t rows, int d) {
+  return x_ml_offset(world, rows, d) + x_align256(size_t(2) * world * rows * 2 * sizeof(float));
+}
+
 // Dynamic (thief) segment slots a launch of `nc` CTAs can create: each steal
 // takes at most kStealChunk tiles, so it adds at most that many segments.
 __host__ __device__ constexpr int64_t dynamic_slot_capacity(int64_t nc) {
@@ -99,7 +125,42 @@ struct DecodeParams {
   int claim_divisor; // the last 1/claim_divisor of each range is claimable
   int64_t dyn_capacity;  // dynamic slots the workspace holds
   float scale_log2;  // log2(e) / sqrt(D)
+  // Peer exchange (kernel instantiated with kExchange): the partial states
+  // go to slot x_rank of every rank's exchange buffer, not state_acc/ml.
+  uint8_t* x_base[kMaxRanks];  // each rank's exchange buffer as mapped here
+  int x_world;
+  int x_rank;
 };
+
+// Number of copies of each partial state a decode stores (one per rank).
+template <bool kExchange>
+__device__ __forceinline__ int partial_copies(const DecodeParams& p) {
+  if constexpr (kExchange) return p.x_world; else return 1;
+}
+
+// This rank's call counter.  Read where a state is stored rather than kept
+// in a register for the whole kernel: it only changes when the last CTA
+// finishes, after every store of the call.
+__device__ __forceinline__ uint32_t x_epoch(const DecodeParams& p) {
+  return *reinterpret_cast<const volatile uint32_t*>(p.x_base[p.x_rank] + kXEpochOffset);
+}
+
+// Destination of copy s of the partial states: the local arrays, or slot
+// `p.x_rank` of rank s's exchange buffer at the parity of the call being
+// produced.
+template <bool kExchange>
+__device__ __forceinline__ float* partial_acc(const DecodeParams& p, int s, int64_t rows, int d) {
+  if constexpr (!kExchange) return p.state_acc;
+  const int64_t par = (x_epoch(p) + 1u) & 1u;
+  return reinterpret_cast<float*>(p.x_base[s] + kXAccOffset) + (par * p.x_world + p.x_rank) * rows * d;
+}
+template <bool kExchange>
+__device__ __forceinline__ float* partial_ml(const DecodeParams& p, int s, int64_t rows, int d) {
+  if constexpr (!kExchange) return p.state_ml;
+  const int64_t par = (x_epoch(p) + 1u) & 1u;
+  return reinterpret_cast<float*>(p.x_base[s] + x_ml_offset(p.x_world, rows, d)) +
+         (par * p.x_world + p.x_rank) * rows * 2;
+}
 
 __device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
 
@@ -250,7 +311,9 @@ __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-template <int D, int kWarps, int kMB, int kStages, bool kTma>
+// kExchange: partial states go to every rank's exchange buffer (a separate
+// instantiation, so the per-rank stores cost the ordinary kernels nothing).
+template <int D, int kWarps, int kMB, int kStages, bool kTma, bool kExchange>
 __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThreads, 1)
     decode_stream_kernel(const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const DecodeParams p) {
@@ -307,6 +370,11 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   __syncthreads();
   // No global memory is touched before the previous grid in the stream is done.
   griddep_wait();
+
+  // Partial-state stores go to the local arrays, or (peer exchange) to this
+  // rank's slot in every rank's exchange buffer.
+  auto acc_dest = [&](int s) -> float* { return partial_acc<kExchange>(p, s, P * G, D); };
+  auto ml_dest = [&](int s) -> float* { return partial_ml<kExchange>(p, s, P * G, D); };
 
   // ------------------------------------------------------------ tile range
   const int64_t nt_uniform = (S + TT - 1) / TT;
@@ -371,15 +439,16 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       for (int64_t b = tid; b < B; b += blockDim.x) {
         if (clamped_len(p, b) != 0) continue;
         for (int64_t row = b * Hq; row < (b + 1) * Hq; ++row) {
-          for (int d = 0; d < D; ++d) {
-            if (p.partial_mode)
-              p.state_acc[row * D + d] = 0.f;
-            else
-              p.out[row * D + d] = __float2bfloat16_rn(0.f);
+          if (!p.partial_mode) {
+            for (int d = 0; d < D; ++d) p.out[row * D + d] = __float2bfloat16_rn(0.f);
+            continue;
           }
-          if (p.partial_mode) {
-            p.state_ml[2 * row] = neg_inf();
-            p.state_ml[2 * row + 1] = 0.f;
+          for (int s = 0; s < partial_copies<kExchange>(p); ++s) {
+            float* a = acc_dest(s);
+            float* ml = ml_dest(s);
+            for (int d = 0; d < D; ++d) a[row * D + d] = 0.f;
+            ml[2 * row] = neg_inf();
+            ml[2 * row + 1] = 0.f;
           }
         }
       }
@@ -708,11 +777,15 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       const int64_t row = q * G + hd;
       const float L = lrun[hi];
       if (p.partial_mode) {
+        for (int s = 0; s < partial_copies<kExchange>(p); ++s) {
+          float* a = acc_dest(s) + row * D + lane * kPer;
 #pragma unroll
-        for (int i = 0; i < kPer; ++i) p.state_acc[row * D + lane * kPer + i] = o[hi][i];
-        if (lane == 0) {
-          p.state_ml[2 * row] = mrun[hi] * kLn2;
-          p.state_ml[2 * row + 1] = L;
+          for (int i = 0; i < kPer; ++i) a[i] = o[hi][i];
+          if (lane == 0) {
+            float* ml = ml_dest(s);
+            ml[2 * row] = mrun[hi] * kLn2;
+            ml[2 * row + 1] = L;
+          }
         }
       } else {
 #pragma unroll
@@ -824,10 +897,13 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       if (complete && !p.partial_mode) {
         p.out[row * D + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
       } else if (complete) {
-        p.state_acc[row * D + d] = O;
-        if (d == 0) {
-          p.state_ml[2 * row] = M * kLn2;
-          p.state_ml[2 * row + 1] = L;
+        for (int s = 0; s < partial_copies<kExchange>(p); ++s) {
+          acc_dest(s)[row * D + d] = O;
+          if (d == 0) {
+            float* ml = ml_dest(s);
+            ml[2 * row] = M * kLn2;
+            ml[2 * row + 1] = L;
+          }
         }
       } else {
         const int64_t srow = slot * G + hd;
@@ -1026,8 +1102,14 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   }
 
   // ------------------------------------------------------------ exit
-  // The last CTA to finish resets the scheduler header for the next call.
-  __threadfence();
+  // The last CTA to finish resets the scheduler header for the next call
+  // and, with a peer exchange, publishes this call's states to every rank.
+  // Peer stores are made visible at system scope before the CTA counts
+  // itself finished, so the last CTA's flags release every CTA's states.
+  if constexpr (kExchange)
+    __threadfence_system();
+  else
+    __threadfence();
   bar();
   if (tid == 0) misc[46] = atomicAdd(p.ws_counters + 1, 1u) == static_cast<uint32_t>(nc - 1);
   bar();
@@ -1043,26 +1125,31 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
     if (tid == 0) {
       p.ws_counters[0] = 0u;
       p.ws_counters[1] = 0u;
+      if constexpr (kExchange) {
+        __threadfence_system();
+        const uint32_t call = x_epoch(p) + 1u;
+        for (int s = 0; s < p.x_world; ++s)
+          st_release_sys_u32(
+              reinterpret_cast<uint32_t*>(p.x_base[s] + kXFlagsOffset) + p.x_rank, call);
+        *reinterpret_cast<volatile uint32_t*>(p.x_base[p.x_rank] + kXEpochOffset) = call;
+      }
     }
   }
 }
 
-// Merges `parts` public partial states (m in natural units) per row into
-// BF16.  One warp per row.  Used for the cross-GPU merge of sequence shards
-// (replaces merge_splits, csrc/decode.cu:169-184).
+// Merges `parts` partial states (m in natural units) of one row into BF16;
+// called by one warp.  Replaces merge_splits (csrc/decode.cu:169-184) for the
+// cross-GPU merge of sequence shards.
 template <int D>
-__global__ void __launch_bounds__(256)
-    merge_states_kernel(const float* __restrict__ acc, int64_t acc_stride,
-                        const float* __restrict__ ml, int64_t ml_stride, int64_t parts,
-                        int64_t rows, __nv_bfloat16* __restrict__ out) {
+__device__ __forceinline__ void merge_row(const float* __restrict__ acc, int64_t acc_stride,
+                                          const float* __restrict__ ml, int64_t ml_stride,
+                                          int64_t parts, int64_t row, __nv_bfloat16* __restrict__ out,
+                                          int lane) {
   constexpr int kPer = D / 32;
   constexpr float kLog2e = 1.4426950408889634f;
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= rows) return;
   float M = neg_inf();
   for (int64_t r = lane; r < parts; r += 32)
-    if (ml[r * ml_stride + 2 * row + 1] > 0.f) M = fmaxf(M, ml[r * ml_stride + 2 * row]);
+    if (__ldcg(ml + r * ml_stride + 2 * row + 1) > 0.f) M = fmaxf(M, __ldcg(ml + r * ml_stride + 2 * row));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   const float Mu = M == neg_inf() ? 0.f : M;
@@ -1070,18 +1157,75 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int i = 0; i < kPer; ++i) O[i] = 0.f;
   for (int64_t r = 0; r < parts; ++r) {
-    const float m = ml[r * ml_stride + 2 * row];
-    const float l = ml[r * ml_stride + 2 * row + 1];
+    const float m = __ldcg(ml + r * ml_stride + 2 * row);
+    const float l = __ldcg(ml + r * ml_stride + 2 * row + 1);
     if (!(l > 0.f)) continue;  // empty part: contributes nothing
     const float f = fast_exp2((m - Mu) * kLog2e);
     L += f * l;
     const float* src = acc + r * acc_stride + row * D + lane * kPer;
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) O[i] += f * src[i];
+    for (int i = 0; i < kPer; ++i) O[i] += f * __ldcg(src + i);
   }
   __nv_bfloat16* dst = out + row * D + lane * kPer;
 #pragma unroll
   for (int i = 0; i < kPer; ++i) dst[i] = __float2bfloat16_rn(L > 0.f ? O[i] / L : 0.f);
+}
+
+// Merges `parts` partial states per row.  One warp per row.
+template <int D>
+__global__ void __launch_bounds__(256)
+    merge_states_kernel(const float* __restrict__ acc, int64_t acc_stride,
+                        const float* __restrict__ ml, int64_t ml_stride, int64_t parts,
+                        int64_t rows, __nv_bfloat16* __restrict__ out) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  merge_row<D>(acc, acc_stride, ml, ml_stride, parts, row, out, threadIdx.x & 31);
+}
+
+// The merge step of a peer exchange (see the layout above), on one rank:
+// waits, bounded by `timeout_ns`, until every rank has delivered the call
+// this rank's decode just completed, then merges the `world` slots of that
+// call's parity per row.  Launched behind the decode kernel with
+// programmatic serialisation; nothing is read before that grid is done.  If
+// the wait gives up, the device error word gets kErrPeerTimeout and the rows
+// are written as zeros.
+template <int D>
+__global__ void __launch_bounds__(256)
+    exchange_merge_kernel(const uint8_t* __restrict__ xbuf, int world, int64_t rows,
+                          __nv_bfloat16* __restrict__ out, uint64_t timeout_ns) {
+  griddep_launch_dependents();
+  griddep_wait();
+  __shared__ int ready;
+  const uint32_t call = *reinterpret_cast<const volatile uint32_t*>(xbuf + kXEpochOffset);
+  if (threadIdx.x == 0) {
+    const uint32_t* flags = reinterpret_cast<const uint32_t*>(xbuf + kXFlagsOffset);
+    int ok = 1;
+    const uint64_t start = global_timer_ns();
+    for (int s = 0; s < world && ok; ++s) {
+      // Flags only grow; a rank one call ahead has already passed `call`.
+      while (static_cast<int32_t>(ld_acquire_sys_u32(flags + s) - call) < 0) {
+        if (global_timer_ns() - start > timeout_ns) {
+          ok = 0;
+          atomicOr(&g_adb_error_flag, kErrPeerTimeout);
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    ready = ok;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  if (!ready) {
+    for (int d = lane; d < D; d += 32) out[row * D + d] = __float2bfloat16_rn(0.f);
+    return;
+  }
+  const int64_t par = call & 1u;
+  const float* acc = reinterpret_cast<const float*>(xbuf + kXAccOffset) + par * world * rows * D;
+  const float* ml = reinterpret_cast<const float*>(xbuf + x_ml_offset(world, rows, D)) + par * world * rows * 2;
+  merge_row<D>(acc, rows * D, ml, rows * 2, world, row, out, lane);
 }
 
 }  // namespace adb

@@ -61,6 +61,7 @@ __device__ int g_adb_error_flag = 0;
 
 constexpr int kErrWaitTimeout = 1;
 constexpr int kErrWorkspace = 2;  // a scheduler counter left its bounds (dirty header)
+constexpr int kErrPeerTimeout = 4;  // a peer's partial states did not arrive in time
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far above any legitimate wait
 
 // Waits for the given phase parity of an mbarrier.  The wait is bounded: if
@@ -157,6 +158,18 @@ __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
 
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue; it must call griddep_wait() before touching this grid's output.
+// System-scope release store / acquire load of a 32-bit flag: the flags that
+// ranks on other GPUs raise in this GPU's memory (and read in theirs).
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* ptr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* ptr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }

@@ -13,8 +13,10 @@
  *     at::Tensor attention_decode_cuda(q, k, v)      csrc/decode.cu:223-258
  * bound to Python as `forward`                       csrc/binding.cpp:3-8
  * with plain pointers, sizes and a caller-supplied stream and workspace, so
- * any FFI (ctypes, cgo, JNI, N-API) can bind it.  No function allocates
- * device memory, synchronises the host or keeps per-call state: every call is
+ * any FFI (ctypes, cgo, JNI, N-API) can bind it.  No decode function
+ * allocates device memory, synchronises the host or keeps per-call state (the
+ * exchange set-up functions at the end are the only ones that allocate or map
+ * memory): every call is
  * stream-ordered and may be captured in a CUDA graph, and concurrent calls on
  * different streams are independent as long as their workspaces differ.
  *
@@ -160,6 +162,52 @@ ADB_API int adb_decode_partial(const void* q, const void* k, const void* v,
 ADB_API int adb_combine(const float* acc, int64_t acc_part_stride, const float* ml,
                         int64_t ml_part_stride, int64_t parts, int64_t rows,
                         int64_t head_dim, void* out, int device, void* stream);
+
+/* ---- Sequence sharding over NVLink peer memory (no reference counterpart:
+ * the reference is single-GPU; this replaces an NCCL all_gather of the
+ * partial states followed by adb_combine).
+ *
+ * Each of `world` ranks (one process per GPU, world <= 8) allocates one
+ * exchange buffer of adb_exchange_size() bytes with adb_exchange_alloc (zeroed),
+ * shares its adb_ipc_handle() with the other ranks through any host channel,
+ * and maps theirs with adb_ipc_open; exchange[r] is then rank r's buffer as
+ * seen from this process (its own buffer at exchange[rank]).  A step is
+ *   adb_decode_exchange(...)   partial decode of this rank's token shard; the
+ *                              kernel stores its states straight into every
+ *                              rank's buffer over NVLink and raises a flag
+ *   adb_exchange_merge(...)    waits (bounded) for every rank's flag, then
+ *                              merges the `world` states per row into BF16
+ * both on one stream; every rank makes the same sequence of calls.  Nothing
+ * synchronises the host, so a step can be captured in a CUDA graph.  The
+ * buffers hold two calls' states (by call parity), so ranks may drift apart
+ * by one call without a barrier.  If a peer's states do not arrive within
+ * `timeout_us`, the merge writes zero rows and sets bit 4 of the device error
+ * word (adb_read_error_flag).  Buffers must stay mapped until every rank has
+ * finished its last step. */
+#define ADB_IPC_HANDLE_BYTES 64
+#define ADB_ERROR_FLAG_PEER_TIMEOUT 4
+
+ADB_API int adb_exchange_size(int64_t rows, int64_t head_dim, int world, size_t* bytes);
+ADB_API int adb_exchange_alloc(size_t bytes, int device, void** buffer);
+ADB_API int adb_exchange_free(void* buffer, int device);
+ADB_API int adb_ipc_handle(void* buffer, int device, unsigned char* handle);
+ADB_API int adb_ipc_open(const unsigned char* handle, int device, void** buffer);
+ADB_API int adb_ipc_close(void* buffer, int device);
+
+/* Partial decode (as adb_decode_partial) whose states go to slot `rank` of
+ * every rank's exchange buffer.  `exchange` holds `world` device pointers. */
+ADB_API int adb_decode_exchange(const void* q, const void* k, const void* v,
+                                const int32_t* seqlens, int64_t batch, int64_t q_heads,
+                                int64_t kv_heads, int64_t kv_len, int64_t head_dim,
+                                void* const* exchange, int world, int rank, void* workspace,
+                                size_t workspace_bytes, unsigned flags, int device,
+                                void* stream);
+
+/* Merge step on this rank's own buffer: out [rows, head_dim] BF16 with
+ * rows = batch * q_heads.  One kernel, launched with programmatic stream
+ * serialisation behind the decode. */
+ADB_API int adb_exchange_merge(const void* exchange, int world, int64_t rows, int64_t head_dim,
+                               void* out, int64_t timeout_us, int device, void* stream);
 
 /* Reads (and optionally clears) the sticky device error word that kernels
  * set when a bounded wait gives up; 0 means no kernel has reported an

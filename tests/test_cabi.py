@@ -96,3 +96,23 @@ def test_python_api_rejects_cpu_inputs():
         attention_decode(q, k, k)
     with pytest.raises(TypeError):
         attention_decode(None, k, k)
+
+
+def test_exchange_arguments_are_checked_on_host():
+    lib = _lib.load_library()
+    size = ctypes.c_size_t(0)
+    assert lib.adb_exchange_size(64, 128, 9, ctypes.byref(size)) == _lib.ADB_ERR_UNSUPPORTED
+    assert lib.adb_exchange_size(64, 96, 2, ctypes.byref(size)) == _lib.ADB_ERR_UNSUPPORTED
+    assert lib.adb_exchange_size(0, 128, 2, ctypes.byref(size)) == _lib.ADB_ERR_INVALID_ARGUMENT
+    assert lib.adb_exchange_size(64, 128, 8, ctypes.byref(size)) == _lib.ADB_OK
+    # 256-byte header, then two parities of 8 ranks' [64, 128] acc and [64, 2] (m, l)
+    assert size.value == 256 + 2 * 8 * 64 * 128 * 4 + 2 * 8 * 64 * 2 * 4
+    rc = lib.adb_decode_exchange(None, None, None, None, 1, 64, 8, 1024, 128, None, 2, 0, None, 0, 0, 0, None)
+    assert rc == _lib.ADB_ERR_INVALID_ARGUMENT and "exchange" in _lib.last_error(lib)
+    bases = (ctypes.c_void_p * 2)(256, 512)
+    rc = lib.adb_decode_exchange(None, None, None, None, 1, 64, 8, 1024, 128, bases, 2, 2, None, 0, 0, 0, None)
+    assert rc == _lib.ADB_ERR_INVALID_ARGUMENT and "rank" in _lib.last_error(lib)
+    rc = lib.adb_exchange_merge(None, 2, 64, 128, None, 1000, 0, None)
+    assert rc == _lib.ADB_ERR_INVALID_ARGUMENT
+    rc = lib.adb_exchange_merge(256, 2, 64, 128, 512, 0, 0, None)
+    assert rc == _lib.ADB_ERR_INVALID_ARGUMENT and "timeout" in _lib.last_error(lib)

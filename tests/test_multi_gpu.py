@@ -1,6 +1,7 @@
-"""Multi-GPU decode over NCCL: sequence sharding (partial states all-gathered
-and merged on every rank, eagerly and replayed from a CUDA graph) and batch
-sharding (no collective).  Needs at least two GPUs; ranks are spawned
+"""Multi-GPU decode: sequence sharding (partial states exchanged through
+NVLink peer memory by the decode kernel itself, and through an NCCL
+all_gather; merged on every rank, eagerly and replayed from a CUDA graph) and
+batch sharding (no collective).  Needs at least two GPUs; ranks are spawned
 processes, one per GPU, with a short process-group timeout so that a failure
 ends in an error, not a hang."""
 
@@ -41,19 +42,29 @@ def _worker(rank, world, port, results):
         S = 16384 + 37
         q, k, v = inputs(device, S, 128, 8, batch=1, hq=64, seed=91)  # same values on every rank
         lo, hi = sharded.token_shard(S, rank, world)
-        step = sharded.SequenceShardedDecode(q, k[:, :, lo:hi].contiguous(), v[:, :, lo:hi].contiguous())
-        out = step().clone()
-        again = step().clone()
         full = ad.attention_decode(q, k, v)
-        torch.cuda.synchronize(device)
-        check(out, full, q, atol=1e-2, rtol=2.0**-7)
-        check(again, out, q, atol=1e-3, rtol=2.0**-7)
-        if rank == 0:
-            check(out, oracle_reference(q, k, v), q)
-        graphed = step.capture()
-        for _ in range(3):
-            check(graphed().clone(), out, q, atol=1e-3, rtol=2.0**-7)
-        step.release()
+        expected = oracle_reference(q, k, v) if rank == 0 else None
+        q2 = inputs(device, 1, 128, 8, batch=1, hq=64, seed=93)[0]
+        full2 = ad.attention_decode(q2, k, v)
+        for transport in ("p2p", "nccl"):
+            step = sharded.SequenceShardedDecode(
+                q.clone(), k[:, :, lo:hi].contiguous(), v[:, :, lo:hi].contiguous(), transport=transport
+            )
+            out = step().clone()
+            again = step().clone()
+            torch.cuda.synchronize(device)
+            check(out, full, q, atol=1e-2, rtol=2.0**-7)
+            check(again, out, q, atol=1e-3, rtol=2.0**-7)
+            if expected is not None:
+                check(out, expected, q)
+            for _ in range(5):  # back to back, no host synchronisation between steps
+                step()
+            check(step.with_query(q2)().clone(), full2, q2, atol=1e-2, rtol=2.0**-7)
+            graphed = step.capture()
+            for query, want in ((q, full), (q2, full2), (q, full)):
+                check(graphed.with_query(query)().clone(), want, query, atol=1e-2, rtol=2.0**-7)
+            step.release()
+        assert ad.read_error_flag(rank) == 0
         # --- batch sharding: each rank decodes its slice of an 8-sequence batch
         q, k, v = inputs(device, 3000, 128, 8, batch=8, hq=32, seed=92)
         sl = sharded.batch_shard(8, rank, world)
