@@ -494,6 +494,9 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   // ------------------------------------------------------------ producer
   if constexpr (kTma) {
     if (warp == kWarps) {
+      // K/V tiles are read exactly once: mark them first to leave L2, so the
+      // segment states that other CTAs merge later stay resident.
+      const uint64_t policy = l2_policy_evict_first();
       int64_t k = 0;  // stage sequence number (lane 0)
       bool ok = true;
       // Lane 0: fill stage k with `m` (and its tile, if it is one).
@@ -510,11 +513,11 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
           const int z = static_cast<int>(m.b * Hkv + m.h);
 #pragma unroll
           for (int h = 0; h < C::kHalves; ++h)
-            tma_load_3d(smem_u32(st + h * C::kBoxBytes), &tm_k, h * 64, y, z, full_bar(s));
+            tma_load_3d(smem_u32(st + h * C::kBoxBytes), &tm_k, h * 64, y, z, full_bar(s), policy);
 #pragma unroll
           for (int h = 0; h < C::kHalves; ++h)
             tma_load_3d(smem_u32(st + (C::kHalves + h) * C::kBoxBytes), &tm_v, h * 64, y, z,
-                        full_bar(s));
+                        full_bar(s), policy);
         } else {
           mbar_arrive(full_bar(s));
         }
@@ -680,8 +683,10 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   // all consumer threads of the CTA whose commit completed the pair.  The
   // segment slots (owners first_cta..last_cta, then every dynamic slot
   // tagged with q, found by a scan shared by all threads) are listed in
-  // shared memory; each warp merges its heads with one segment per lane for
-  // the weights and one row per load for the sums.
+  // shared memory.  Each warp merges its heads 32 segments at a time: lane j
+  // loads segment j's (m, l) of every head (one round trip for all the
+  // weights), then the accumulator rows of several segments and of all its
+  // heads are loaded together and folded in.
   auto merge_pair = [&](int64_t q, int64_t first, int64_t last, int64_t n_thieves) {
     __threadfence();
     constexpr int kPer = D / 32;
@@ -718,54 +723,77 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
           mg_list[atomicAdd(reinterpret_cast<int*>(misc + 48), 1)] = static_cast<int32_t>(nc + P + d);
       bar();
       const int n = static_cast<int>(misc[48]);
+      constexpr int H = C::kHeadsPerWarp;
+      constexpr int kU = 4;  // segments whose rows are in flight together
+      for (int c0 = 0; c0 < n; c0 += 32) {
+        const int cn = n - c0 < 32 ? n - c0 : 32;
+        // Lane j holds segment c0 + j's (m, l) of each of this warp's heads:
+        // one round trip for the chunk's weights.
+        float w[H];
+        {
+          float mj[H], lj[H];
+          const int64_t sb = lane < cn ? static_cast<int64_t>(mg_list[c0 + lane]) * G : 0;
 #pragma unroll
-      for (int hi = 0; hi < C::kHeadsPerWarp; ++hi) {
-        const int hd = warp + hi * kWarps;
-        if (hd >= G) break;
-        // Four segments at a time: their (m, l) and this lane's slice of
-        // their accumulator rows are loaded together (one round trip), then
-        // folded into the running state.
-        for (int j0 = 0; j0 < n; j0 += 4) {
-          float mj[4], lj[4], x[4][kPer];
+          for (int hi = 0; hi < H; ++hi) {
+            const int hd = warp + hi * kWarps;
+            mj[hi] = neg_inf();
+            lj[hi] = 0.f;
+            if (hd < G && lane < cn) {
+              const float2 ml2 = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + 2 * (sb + hd)));
+              mj[hi] = ml2.x;
+              lj[hi] = ml2.y;
+            }
+          }
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            mj[u] = neg_inf();
-            lj[u] = 0.f;
+          for (int hi = 0; hi < H; ++hi) {
+            // empty owner states (l = 0) hold no accumulator: weight 0
+            float cm = lj[hi] > 0.f ? mj[hi] : neg_inf();
 #pragma unroll
-            for (int i = 0; i < kPer; ++i) x[u][i] = 0.f;
-            if (j0 + u < n) {
-              const int64_t srow = static_cast<int64_t>(mg_list[j0 + u]) * G + hd;
-              const float2 ml2 = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + 2 * srow));
-              mj[u] = ml2.x;
-              lj[u] = ml2.y;
-              const float* row = p.ws_acc + srow * D + lane * kPer;
-              if constexpr (kPer == 4) {
-                const float4 v4 = __ldcg(reinterpret_cast<const float4*>(row));
-                x[u][0] = v4.x; x[u][1] = v4.y; x[u][2] = v4.z; x[u][3] = v4.w;
-              } else {
-                const float2 v2 = __ldcg(reinterpret_cast<const float2*>(row));
-                x[u][0] = v2.x; x[u][1] = v2.y;
+            for (int o2 = 16; o2 > 0; o2 >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o2));
+            const float mnew = fmaxf(mrun[hi], cm);
+            const float mu = mnew == neg_inf() ? 0.f : mnew;
+            const float alpha = fast_exp2(mrun[hi] - mu);
+            w[hi] = lj[hi] > 0.f ? fast_exp2(mj[hi] - mu) : 0.f;
+            float ls = w[hi] * lj[hi];
+#pragma unroll
+            for (int o2 = 16; o2 > 0; o2 >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o2);
+            lrun[hi] = lrun[hi] * alpha + ls;
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) o[hi][i] *= alpha;
+            mrun[hi] = mnew;
+          }
+        }
+        // Accumulator rows: kU segments of every head of this warp at once.
+        for (int j0 = 0; j0 < cn; j0 += kU) {
+          float x[kU][H][kPer], wj[kU][H];
+#pragma unroll
+          for (int u = 0; u < kU; ++u) {
+            const int j = j0 + u;
+            const int64_t sb = static_cast<int64_t>(mg_list[c0 + (j < cn ? j : 0)]) * G;
+#pragma unroll
+            for (int hi = 0; hi < H; ++hi) {
+              const int hd = warp + hi * kWarps;
+              wj[u][hi] = __shfl_sync(0xffffffffu, w[hi], j & 31);
+#pragma unroll
+              for (int i = 0; i < kPer; ++i) x[u][hi][i] = 0.f;
+              if (j < cn && hd < G && wj[u][hi] > 0.f) {
+                const float* row = p.ws_acc + (sb + hd) * D + lane * kPer;
+                if constexpr (kPer == 4) {
+                  const float4 v4 = __ldcg(reinterpret_cast<const float4*>(row));
+                  x[u][hi][0] = v4.x; x[u][hi][1] = v4.y; x[u][hi][2] = v4.z; x[u][hi][3] = v4.w;
+                } else {
+                  const float2 v2 = __ldcg(reinterpret_cast<const float2*>(row));
+                  x[u][hi][0] = v2.x; x[u][hi][1] = v2.y;
+                }
               }
             }
           }
-          float mnew = mrun[hi];
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            if (lj[u] > 0.f) mnew = fmaxf(mnew, mj[u]);
-          const float mu = mnew == neg_inf() ? 0.f : mnew;
-          const float alpha = fast_exp2(mrun[hi] - mu);
-          lrun[hi] *= alpha;
+          for (int u = 0; u < kU; ++u)
 #pragma unroll
-          for (int i = 0; i < kPer; ++i) o[hi][i] *= alpha;
+            for (int hi = 0; hi < H; ++hi)
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            // empty owner states (l = 0) hold no accumulator; skip them
-            const float w = lj[u] > 0.f ? fast_exp2(mj[u] - mu) : 0.f;
-            lrun[hi] += w * lj[u];
-#pragma unroll
-            for (int i = 0; i < kPer; ++i) o[hi][i] += w > 0.f ? w * x[u][i] : 0.f;
-          }
-          mrun[hi] = mnew;
+              for (int i = 0; i < kPer; ++i) o[hi][i] += wj[u][hi] * x[u][hi][i];
         }
       }
       bar();  // the list is refilled next pass

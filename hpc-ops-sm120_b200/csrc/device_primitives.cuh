@@ -91,13 +91,21 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
 // ---------------------------------------------------------------- TMA
 // 3-D tiled bulk tensor load global -> shared, completion via mbarrier
 // transaction bytes.  No multicast (plain CTA-local load).
+// The copy carries an L2 cache-eviction policy (createpolicy).
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y,
-                                            int z, uint32_t bar) {
+                                            int z, uint32_t bar, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
       : "memory");
+}
+
+// L2 policy for data read once: evict it first (all of the access).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
 }
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
