@@ -138,26 +138,25 @@ __device__ __forceinline__ int partial_copies(const DecodeParams& p) {
   if constexpr (kExchange) return p.x_world; else return 1;
 }
 
-// This rank's call counter.  Read where a state is stored rather than kept
-// in a register for the whole kernel: it only changes when the last CTA
-// finishes, after every store of the call.
+// This rank's call counter (it only changes when the last CTA finishes,
+// after every store of the call).
 __device__ __forceinline__ uint32_t x_epoch(const DecodeParams& p) {
   return *reinterpret_cast<const volatile uint32_t*>(p.x_base[p.x_rank] + kXEpochOffset);
 }
 
 // Destination of copy s of the partial states: the local arrays, or slot
-// `p.x_rank` of rank s's exchange buffer at the parity of the call being
-// produced.
+// `p.x_rank` of rank s's exchange buffer at parity `par` (of the call being
+// produced).
 template <bool kExchange>
-__device__ __forceinline__ float* partial_acc(const DecodeParams& p, int s, int64_t rows, int d) {
+__device__ __forceinline__ float* partial_acc(const DecodeParams& p, int s, int64_t par,
+                                              int64_t rows, int d) {
   if constexpr (!kExchange) return p.state_acc;
-  const int64_t par = (x_epoch(p) + 1u) & 1u;
   return reinterpret_cast<float*>(p.x_base[s] + kXAccOffset) + (par * p.x_world + p.x_rank) * rows * d;
 }
 template <bool kExchange>
-__device__ __forceinline__ float* partial_ml(const DecodeParams& p, int s, int64_t rows, int d) {
+__device__ __forceinline__ float* partial_ml(const DecodeParams& p, int s, int64_t par,
+                                             int64_t rows, int d) {
   if constexpr (!kExchange) return p.state_ml;
-  const int64_t par = (x_epoch(p) + 1u) & 1u;
   return reinterpret_cast<float*>(p.x_base[s] + x_ml_offset(p.x_world, rows, d)) +
          (par * p.x_world + p.x_rank) * rows * 2;
 }
@@ -336,7 +335,7 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   // misc[0..32]: scan scratch; misc[40..43]: batches / bases of the first and
   // last tile; misc[44]: dynamic slot of a thief flush; misc[46]: broadcast
   // flag; misc[47]: dynamic slots in use; misc[48]: merge segment count;
-  // misc[50]: abort flag
+  // misc[50]: abort flag; misc[52]: parity of the exchange slots written
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 50);
   // merge slot list, aliased on fl_acc (see StreamCfg)
   int32_t* mg_list = reinterpret_cast<int32_t*>(fl_acc);
@@ -372,9 +371,18 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   griddep_wait();
 
   // Partial-state stores go to the local arrays, or (peer exchange) to this
-  // rank's slot in every rank's exchange buffer.
-  auto acc_dest = [&](int s) -> float* { return partial_acc<kExchange>(p, s, P * G, D); };
-  auto ml_dest = [&](int s) -> float* { return partial_ml<kExchange>(p, s, P * G, D); };
+  // rank's slot in every rank's exchange buffer, at the parity of the call
+  // being produced (read once here and kept in shared memory, misc[52]).
+  if constexpr (kExchange) {
+    if (tid == 0) misc[52] = (x_epoch(p) + 1u) & 1u;
+    __syncthreads();
+  }
+  auto acc_dest = [&](int s) -> float* {
+    return partial_acc<kExchange>(p, s, kExchange ? misc[52] : 0, P * G, D);
+  };
+  auto ml_dest = [&](int s) -> float* {
+    return partial_ml<kExchange>(p, s, kExchange ? misc[52] : 0, P * G, D);
+  };
 
   // ------------------------------------------------------------ tile range
   const int64_t nt_uniform = (S + TT - 1) / TT;
@@ -1131,13 +1139,11 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
 
   // ------------------------------------------------------------ exit
   // The last CTA to finish resets the scheduler header for the next call
-  // and, with a peer exchange, publishes this call's states to every rank.
-  // Peer stores are made visible at system scope before the CTA counts
-  // itself finished, so the last CTA's flags release every CTA's states.
-  if constexpr (kExchange)
-    __threadfence_system();
-  else
-    __threadfence();
+  // and, with a peer exchange, publishes this call's states to every rank:
+  // each CTA's stores (peer ones included) are released at GPU scope before
+  // it counts itself finished; the last CTA, having observed every count,
+  // fences at system scope and raises the flags, which releases them all.
+  __threadfence();
   bar();
   if (tid == 0) misc[46] = atomicAdd(p.ws_counters + 1, 1u) == static_cast<uint32_t>(nc - 1);
   bar();
