@@ -716,13 +716,23 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
     const int64_t per_pass = C::kMergeList - n_owner;
     const int64_t passes = n_tag > 0 ? (n_tag + per_pass - 1) / per_pass : 1;
     for (int64_t r = 0; r < passes; ++r) {
-      if (tid == 0) {
+      if (warp == 0) {
+        // Owner slots first..last in order (warp-parallel, order kept with a
+        // ballot); with at least as many tiles as CTAs every range is
+        // non-empty and no division is needed.
         int n = 0;
-        if (r == 0)
-          for (int64_t cc = first; cc <= last; ++cc)
-            if (cc * nt_total / nc != (cc + 1) * nt_total / nc)
-              mg_list[n++] = static_cast<int32_t>(cc + q);
-        misc[48] = n;
+        if (r == 0) {
+          const bool all_owned = nc <= nt_total;
+          for (int64_t base = first; base <= last; base += 32) {
+            const int64_t cc = base + lane;
+            const bool take =
+                cc <= last && (all_owned || cc * nt_total / nc != (cc + 1) * nt_total / nc);
+            const unsigned bal = __ballot_sync(0xffffffffu, take);
+            if (take) mg_list[n + __popc(bal & ((1u << lane) - 1u))] = static_cast<int32_t>(cc + q);
+            n += __popc(bal);
+          }
+        }
+        if (lane == 0) misc[48] = n;
       }
       bar();
       const int64_t d_end = (r + 1) * per_pass < n_tag ? (r + 1) * per_pass : n_tag;
