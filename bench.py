@@ -52,7 +52,10 @@ def parse_args():
     p.add_argument("--steps", type=int, default=2000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--config", default="cfg2", choices=("cfg1", "cfg2", "cfg3", "cfg4", "cfg5"))
-    p.add_argument("--impl", default="b200", choices=("b200", "reference"))
+    p.add_argument("--impl", default="b200", choices=("b200", "reference", "ref-kernel", "sdpa"),
+                   help="b200: this library; reference: the reference's FP32 algorithm on host cores; "
+                        "ref-kernel: the reference's CUDA kernel rebuilt for sm_100a (baseline/build_ref_kernel.py); "
+                        "sdpa: torch scaled_dot_product_attention (comparison arms, 1 GPU)")
     p.add_argument("--transport", default="p2p", choices=("p2p", "nccl"),
                    help="cfg4 at N>1: state exchange through NVLink peer memory (p2p) or an NCCL all_gather")
     p.add_argument("--seed", type=int, default=2026)
@@ -486,6 +489,105 @@ def run_gpu_arm(args):
     return 0
 
 
+def run_comparison_arm(args):
+    """Another GPU implementation of the same step on the same inputs, timed
+    like this library's arm (events around --steps back-to-back calls): the
+    reference's own kernel rebuilt for sm_100a, or torch SDPA.  One GPU; other
+    ranks exit."""
+    rank, world, local_rank = dist_env()
+    if rank != 0:
+        return 0
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    import attention_decode as ad
+    from attention_decode.workloads import BASELINE_CONFIGS
+
+    cfg = BASELINE_CONFIGS[args.config]
+
+    def unavailable(why):
+        print(json.dumps({"impl": args.impl, "config": cfg.as_dict(), "unavailable": why}), flush=True)
+        return 0
+
+    if world > 1:
+        return unavailable("comparison arms run on one GPU")
+    q, k, v, seqlens = cfg.make_inputs(device, seed=args.seed + 1009 * rank)
+    if args.impl == "ref-kernel":
+        sys.path.insert(0, os.path.join(ROOT, "baseline"))
+        import importlib.util
+
+        from build_ref_kernel import MODULE, module_path
+
+        path = module_path()
+        if not path.is_file():
+            return unavailable(f"{path} not built (python baseline/build_ref_kernel.py --reference-root <checkout>)")
+        group = cfg.query_heads // cfg.kv_heads
+        if seqlens is not None:
+            return unavailable("reference kernel has no sequence lengths (csrc/decode.cu:223-258)")
+        if group not in (1, 4):
+            return unavailable(f"reference kernel supports GQA groups 1 and 4, not {group} (csrc/decode.cu:239)")
+        if k.numel() > 2**31 - 1:
+            return unavailable("reference kernel limits tensors to INT_MAX elements (csrc/decode.cu:231)")
+        spec = importlib.util.spec_from_file_location(MODULE, str(path))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+
+        def step():
+            return mod.forward(q, k, v)
+
+        label = "reference csrc/decode.cu rebuilt for sm_100a (capability gate relaxed, otherwise unchanged)"
+    else:
+        import torch.nn.functional as F
+
+        mask = None
+        if seqlens is not None:
+            mask = (torch.arange(cfg.kv_len, device=device)[None, :] < seqlens[:, None].long())[:, None, None, :]
+
+        def step():
+            return F.scaled_dot_product_attention(q, k, v, attn_mask=mask, enable_gqa=True)
+
+        label = "torch.nn.functional.scaled_dot_product_attention(enable_gqa=True" + (", boolean padding mask)" if mask is not None else ")")
+    out = step()
+    want = ad.attention_decode(q, k, v, seqlens)
+    torch.cuda.synchronize(device)
+    max_err = float((out.float() - want.float()).abs().max())
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    sampler = ClockSampler(device)
+    sampler.start()
+    time.sleep(0.3)
+    stream = torch.cuda.current_stream(device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    stop.record(stream)
+    torch.cuda.synchronize(device)
+    clocks = sampler.stop()
+    ms_step = start.elapsed_time(stop) / args.steps
+    total_bytes = cfg.algorithmic_bytes(seqlens)
+    line = {
+        "impl": args.impl,
+        "metric": METRIC,
+        "value": total_bytes / (ms_step * 1e-3) / 1e9,
+        "unit": "GB/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "us_per_step": ms_step * 1e3,
+        "higher_is_better": True,
+        "dtype": "bf16",
+        "config": cfg.as_dict(),
+        "implementation": label,
+        "max_abs_diff_vs_b200": max_err,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def ctypes_count(lib) -> int:
     import ctypes
 
@@ -498,6 +600,8 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.impl in ("ref-kernel", "sdpa"):
+        return run_comparison_arm(args)
     return run_gpu_arm(args)
 
 
