@@ -43,6 +43,7 @@ import torch  # noqa: E402
 
 HBM_FALLBACK_GBS = 6650.0
 NOMINAL_HBM_GBS = 8000.0
+L2_BYTES = 126 * 1000 * 1000
 METRIC = "decode achieved HBM GB/s (algorithmic valid K+V + Q + O bytes / step time)"
 
 
@@ -59,6 +60,8 @@ def parse_args():
     p.add_argument("--transport", default="p2p", choices=("p2p", "nccl"),
                    help="cfg4 at N>1: state exchange through NVLink peer memory (p2p) or an NCCL all_gather")
     p.add_argument("--seed", type=int, default=2026)
+    p.add_argument("--graph", type=int, default=0,
+                   help="also time replays of a CUDA graph holding this many steps (0: off)")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle timing")
     p.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end pass (default: --steps, at most 500)")
     args = p.parse_args()
@@ -309,15 +312,23 @@ def run_gpu_arm(args):
         )
     else:
         bytes_per_rank = cfg.algorithmic_bytes(seqlens)
+        sets, kv_total = rotation_sets(cfg, device, args.seed + 1009 * rank, (q, k, v))
+        n_sets = len(sets)
+        rotation = [0]
 
         def step():
-            return ad.attention_decode(q, k, v, seqlens)
+            i = rotation[0]
+            rotation[0] = (i + 1) % n_sets
+            qq, kk, vv = sets[i]
+            return ad.attention_decode(qq, kk, vv, seqlens)
 
         scaling = "weak"
         parallelism = f"batch-shard dp{world} (no collective)" if world > 1 else "single GPU"
 
     # Correctness gate on a subset of sequences (full rows, CPU oracle).
     out = step()
+    if not sequence_sharded:
+        rotation[0] = 0
     torch.cuda.synchronize(device)
     check = {"rows_checked": 0, "max_abs_err": None}
     if not sequence_sharded or rank == 0:
@@ -395,6 +406,35 @@ def run_gpu_arm(args):
     achieved = kernel_bytes / (kernel_ms * 1e-3) / 1e9
     traffic = profile_traffic(f"{cfg.name}_decode_stream_kernel")
 
+    # ---- optional: the same steps replayed from a CUDA graph
+    graph_line = None
+    if args.graph > 0 and not sequence_sharded:
+        gstream = torch.cuda.Stream(device=device)
+        gstream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(gstream):
+            for _ in range(3):
+                step()
+        torch.cuda.current_stream(device).wait_stream(gstream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=gstream):
+            for _ in range(args.graph):
+                step()
+        for _ in range(3):
+            graph.replay()
+        replays = max(1, args.steps // args.graph)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(device)
+        g0.record(stream)
+        for _ in range(replays):
+            graph.replay()
+        g1.record(stream)
+        torch.cuda.synchronize(device)
+        g_ms = g0.elapsed_time(g1) / (replays * args.graph)
+        g_ms = max_over_ranks(g_ms, world, device)
+        graph_line = {"steps_per_graph": args.graph, "replays": replays, "us_per_step": g_ms * 1e3,
+                      "value": total_bytes / (g_ms * 1e-3) / 1e9}
+        del graph
+
     # ---- end to end through the public API: pinned H2D of Q, decode, D2H of O
     e2e_steps = args.e2e_steps or min(args.steps, 500)
     q_host = q.cpu().pin_memory()
@@ -435,6 +475,11 @@ def run_gpu_arm(args):
         gbs, desc, _ = cpu_oracle_throughput(q, k, v, seqlens, cfg, budget_s=10.0)
         cpu = {"value": gbs, "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port", "sample": desc}
 
+    if sequence_sharded or n_sets == 1:
+        l2_note = "KV cache larger than the 126 MB L2: every step streams from HBM, no flush needed"
+    else:
+        l2_note = (f"KV cache smaller than L2: steps rotate among {n_sets} independent input sets "
+                   f"({n_sets * kv_total / 1e6:.0f} MB > 2 x L2), so every step streams from HBM")
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -450,7 +495,7 @@ def run_gpu_arm(args):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) bf16 Q/K/V" + (", K ~ N(0,8^2) with x50 spikes" if cfg.extreme else "") + ")",
-            "config": dict(cfg.as_dict(), parallelism=parallelism, l2="KV cache larger than the 126 MB L2: no flush needed" if cfg.name != "cfg1" else "4 MiB KV is L2-resident between steps (no flush)"),
+            "config": dict(cfg.as_dict(), parallelism=parallelism, l2=l2_note),
             "pct_of_8tbs": 100.0 * (total_bytes / (ms_step * 1e-3) / 1e9) / (NOMINAL_HBM_GBS * (world if not sequence_sharded else world)),
             "roofline": {
                 "bound": "hbm",
@@ -475,6 +520,7 @@ def run_gpu_arm(args):
                 "note": "per step: pinned H2D of Q, attention_decode() through the C ABI, D2H of O, host sync; the KV cache is resident decode state",
             },
             "gpu_launches": launches_timed,
+            "graph": graph_line,
             "clocks": clocks,
             "correctness": check,
         }
@@ -487,6 +533,21 @@ def run_gpu_arm(args):
         dist.destroy_process_group()
     del launches0
     return 0
+
+
+def rotation_sets(cfg, device, seed, first):
+    """Input sets that steps rotate among.  A KV cache smaller than twice the
+    L2 would be served from L2 on the next step, so enough independent seeded
+    sets are made that every step streams from HBM (the KV rotation of the
+    reference's bench_extreme.py:103-107).  Returns (sets, KV bytes per set)."""
+    q, k, v = first
+    kv_total = 2 * k.numel() * k.element_size()
+    n_sets = 1 if kv_total >= 2 * L2_BYTES else min(64, -(-2 * L2_BYTES // kv_total))
+    sets = [(q, k, v)]
+    for i in range(1, n_sets):
+        qi, ki, vi, _ = cfg.make_inputs(device, seed=seed + 7919 * i)
+        sets.append((qi, ki, vi))
+    return sets, kv_total
 
 
 def run_comparison_arm(args):
@@ -531,8 +592,8 @@ def run_comparison_arm(args):
         mod = importlib.util.module_from_spec(spec)
         spec.loader.exec_module(mod)
 
-        def step():
-            return mod.forward(q, k, v)
+        def call(qq, kk, vv):
+            return mod.forward(qq, kk, vv)
 
         label = "reference csrc/decode.cu rebuilt for sm_100a (capability gate relaxed, otherwise unchanged)"
     else:
@@ -542,14 +603,22 @@ def run_comparison_arm(args):
         if seqlens is not None:
             mask = (torch.arange(cfg.kv_len, device=device)[None, :] < seqlens[:, None].long())[:, None, None, :]
 
-        def step():
-            return F.scaled_dot_product_attention(q, k, v, attn_mask=mask, enable_gqa=True)
+        def call(qq, kk, vv):
+            return F.scaled_dot_product_attention(qq, kk, vv, attn_mask=mask, enable_gqa=True)
 
         label = "torch.nn.functional.scaled_dot_product_attention(enable_gqa=True" + (", boolean padding mask)" if mask is not None else ")")
-    out = step()
+    out = call(q, k, v)
     want = ad.attention_decode(q, k, v, seqlens)
     torch.cuda.synchronize(device)
     max_err = float((out.float() - want.float()).abs().max())
+    sets, _ = rotation_sets(cfg, device, args.seed + 1009 * rank, (q, k, v))
+    rotation = [0]
+
+    def step():
+        i = rotation[0]
+        rotation[0] = (i + 1) % len(sets)
+        return call(*sets[i])
+
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(device)
@@ -581,6 +650,7 @@ def run_comparison_arm(args):
         "dtype": "bf16",
         "config": cfg.as_dict(),
         "implementation": label,
+        "input_sets": len(sets),
         "max_abs_diff_vs_b200": max_err,
         "clocks": clocks,
     }
