@@ -22,6 +22,7 @@ from ._lib import AttentionDecodeError
 
 __all__ = [
     "attention_decode",
+    "attention_decode_paged",
     "attention_decode_partial",
     "combine_partials",
     "workspace_bytes",
@@ -212,6 +213,79 @@ def attention_decode(q, k, v, seqlens=None):
     _validate(q, k, v, seqlens)
     out = _torch().empty_like(q)
     _launch(q, k, v, seqlens, out=out)
+    return out
+
+
+_PAGED_LAYOUTS = {"HND": _lib.ADB_PAGED_HND, "NHD": _lib.ADB_PAGED_NHD}
+
+
+def attention_decode_paged(q, k_cache, v_cache, block_table, seqlens, *, layout="HND"):
+    """Decode over a paged KV cache (the layout of a serving engine's cache;
+    the reference takes contiguous caches only).
+
+    Q: [B,Hq,1,D] BF16.  ``k_cache``/``v_cache``: pools of pages, BF16,
+    ``layout="HND"``: [num_blocks, Hkv, page_size, D] or ``"NHD"``:
+    [num_blocks, page_size, Hkv, D]; page_size a power of two from 8.
+    ``block_table``: int32 [B, max_blocks] (page j of sequence b is
+    block_table[b, j]; rows may be padded with any value past a sequence's
+    last page).  ``seqlens``: int32 [B], clamped to [0, max_blocks *
+    page_size].  Returns a new [B,Hq,1,D] BF16 tensor.  Uses the current
+    CUDA stream.
+    """
+    torch = _torch()
+    if layout not in _PAGED_LAYOUTS:
+        raise ValueError(f"layout must be 'HND' or 'NHD' (got {layout!r})")
+    Tensor = torch.Tensor
+    for name, t in (("Q", q), ("k_cache", k_cache), ("v_cache", v_cache), ("block_table", block_table), ("seqlens", seqlens)):
+        if not isinstance(t, Tensor):
+            raise TypeError(f"{name} must be a tensor")
+        if not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor")
+        if t.device != q.device:
+            _fail(f"{name} must be on Q's device")
+    bf16 = torch.bfloat16
+    if q.dtype is not bf16 or k_cache.dtype is not bf16 or v_cache.dtype is not bf16:
+        _fail("Q/K/V dtype must be BF16 (bfloat16)")
+    if q.dim() != 4 or k_cache.dim() != 4 or v_cache.dim() != 4:
+        _fail("Q and the caches must have rank four")
+    if not (q.is_contiguous() and k_cache.is_contiguous() and v_cache.is_contiguous()):
+        _fail("Q/K/V must be contiguous")
+    if k_cache.shape != v_cache.shape:
+        _fail("K/V cache shapes must match")
+    if q.shape[2] != 1:
+        _fail("query length must be 1")
+    if layout == "HND":
+        num_blocks, kv_heads, page_size, head_dim = k_cache.shape
+    else:
+        num_blocks, page_size, kv_heads, head_dim = k_cache.shape
+    batch, q_heads = q.shape[0], q.shape[1]
+    if q.shape[3] != head_dim:
+        _fail("Q/K/V batch and head dimension must match")
+    if q_heads % kv_heads != 0:
+        _fail("query heads must be divisible by KV heads")
+    if q_heads // kv_heads not in _GROUPS:
+        _fail("supported GQA group sizes are 1, 4 and 8")
+    if head_dim not in _DIMS:
+        _fail("head dimension must be 64 or 128")
+    if block_table.dtype != torch.int32 or block_table.dim() != 2 or block_table.shape[0] != batch or block_table.stride(1) != 1:
+        _fail("block_table must be an int32 [batch, max_blocks] tensor with contiguous rows")
+    if seqlens.dtype != torch.int32 or seqlens.dim() != 1 or seqlens.shape[0] != batch or not seqlens.is_contiguous():
+        _fail("seqlens must be a contiguous int32 [batch] tensor")
+    lib = _lib.load_library()
+    device = q.device.index if q.device.index is not None else torch.cuda.current_device()
+    max_blocks = block_table.shape[1]
+    nbytes, header = workspace_bytes(batch, q_heads, kv_heads, max_blocks * page_size, head_dim, True, device)
+    stream = torch._C._cuda_getCurrentRawStream(device)
+    workspace, flags = _workspace(q.device, device, stream, nbytes, header)
+    out = torch.empty_like(q)
+    _lib.check(
+        lib,
+        lib.adb_decode_paged(
+            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(), block_table.stride(0),
+            seqlens.data_ptr(), out.data_ptr(), batch, q_heads, kv_heads, head_dim, num_blocks, page_size,
+            max_blocks, _PAGED_LAYOUTS[layout], workspace.data_ptr(), workspace.numel(), flags, device, stream,
+        ),
+    )
     return out
 
 

@@ -26,6 +26,8 @@ ADB_ERR_WORKSPACE = 4
 ADB_ERR_CUDA = 5
 ADB_FLAG_HEADER_ZEROED = 1
 ADB_IPC_HANDLE_BYTES = 64
+ADB_PAGED_HND = 0
+ADB_PAGED_NHD = 1
 ADB_ERROR_FLAG_PEER_TIMEOUT = 4
 
 STATUS_NAMES = {
@@ -58,6 +60,11 @@ PROTOTYPES = {
     "adb_decode_partial": (
         _int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _size, _uint, _int, _vp],
+    ),
+    "adb_decode_paged": (
+        _int,
+        [_vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int,
+         _vp, _size, _uint, _int, _vp],
     ),
     "adb_decode_no_alloc": (
         _int,

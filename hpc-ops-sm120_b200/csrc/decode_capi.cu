@@ -215,13 +215,34 @@ int encode_kv_map(CUtensorMap* map, const void* base, int64_t pairs, int64_t S, 
   return ADB_OK;
 }
 
+// 4-D map over a paged pool laid out [blocks][page][kv_heads][D] bf16 (NHD);
+// a box is 64 columns x 1 head x `rows` tokens x 1 block.
+int encode_nhd_map(CUtensorMap* map, const void* base, int64_t blocks, int64_t page,
+                   int64_t heads, int64_t D, int rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  int rc = get_encoder(&encode);
+  if (rc != ADB_OK) return rc;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(heads),
+                        static_cast<cuuint64_t>(page), static_cast<cuuint64_t>(blocks)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(heads * D * 2),
+                           static_cast<cuuint64_t>(page * heads * D * 2)};
+  cuuint32_t box[4] = {64u, 1u, static_cast<cuuint32_t>(rows), 1u};
+  cuuint32_t elem[4] = {1u, 1u, 1u, 1u};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
+                      strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ADB_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
+  return ADB_OK;
+}
+
 // Encoded descriptors of the last few K/V tensors this thread used: a decode
 // loop passes the same cache buffers every step, and re-encoding costs host
 // time on every call.
 struct MapCacheEntry {
   const void* base = nullptr;
-  int64_t pairs = 0, S = 0, D = 0;
+  int64_t pairs = 0, S = 0, D = 0, heads = 0;
   int tile_tokens = 0;
+  int layout = 0;  // 0: 3-D [rows][S][D]; 1: 4-D NHD pages (pairs = blocks, S = page)
   CUtensorMap map;
 };
 constexpr int kMapCacheEntries = 8;
@@ -229,14 +250,15 @@ thread_local MapCacheEntry t_map_cache[kMapCacheEntries];
 thread_local int t_map_cache_next = 0;
 
 int kv_map(CUtensorMap* map, const void* base, int64_t pairs, int64_t S, int64_t D,
-           int tile_tokens) {
+           int tile_tokens, int layout = 0, int64_t heads = 0) {
   for (const MapCacheEntry& e : t_map_cache)
     if (e.base == base && e.pairs == pairs && e.S == S && e.D == D &&
-        e.tile_tokens == tile_tokens) {
+        e.tile_tokens == tile_tokens && e.layout == layout && e.heads == heads) {
       *map = e.map;
       return ADB_OK;
     }
-  const int rc = encode_kv_map(map, base, pairs, S, D, tile_tokens);
+  const int rc = layout == 0 ? encode_kv_map(map, base, pairs, S, D, tile_tokens)
+                             : encode_nhd_map(map, base, pairs, S, heads, D, tile_tokens);
   if (rc != ADB_OK) return rc;
   MapCacheEntry& e = t_map_cache[t_map_cache_next];
   t_map_cache_next = (t_map_cache_next + 1) % kMapCacheEntries;
@@ -244,7 +266,9 @@ int kv_map(CUtensorMap* map, const void* base, int64_t pairs, int64_t S, int64_t
   e.pairs = pairs;
   e.S = S;
   e.D = D;
+  e.heads = heads;
   e.tile_tokens = tile_tokens;
+  e.layout = layout;
   e.map = *map;
   return ADB_OK;
 }
@@ -349,6 +373,15 @@ struct DeviceGuard {
 
 bool is_aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
+// A paged K/V cache (adb_decode_paged): pools of 2^page_shift-token pages.
+struct PagedArgs {
+  const int32_t* block_table;
+  int64_t bt_stride;
+  int64_t num_blocks;
+  int page_shift;
+  int layout;  // ADB_PAGED_HND or ADB_PAGED_NHD
+};
+
 // Destinations of a decode whose partial states go to every rank's exchange
 // buffer (adb_decode_exchange).
 struct ExchangeArgs {
@@ -361,7 +394,7 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
                float* state_acc, float* state_ml, int64_t batch, int64_t q_heads, int64_t kv_heads,
                int64_t kv_len, int64_t head_dim, void* workspace, size_t workspace_bytes,
                unsigned flags, int device, void* stream_ptr, bool allow_steal = true,
-               const ExchangeArgs* exchange = nullptr) {
+               const ExchangeArgs* exchange = nullptr, const PagedArgs* paged = nullptr) {
   Shape s;
   int rc = check_shape(batch, q_heads, kv_heads, kv_len, head_dim, &s);
   if (rc != ADB_OK) return rc;
@@ -377,6 +410,8 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
   rc = probe_device(device, &st);
   if (rc != ADB_OK) return rc;
   const bool tma = is_aligned(k, 16) && is_aligned(v, 16);
+  if (paged != nullptr && !tma)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "paged K/V caches must be 16-byte aligned");
   Plan plan;
   rc = make_plan(s, seqlens != nullptr, tma, st, &plan, allow_steal);
   if (rc != ADB_OK) return rc;
@@ -390,7 +425,19 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
   CUtensorMap tm_k, tm_v;
   std::memset(&tm_k, 0, sizeof(tm_k));
   std::memset(&tm_v, 0, sizeof(tm_v));
-  if (var.tma) {
+  if (var.tma && paged != nullptr) {
+    // One box is a page-sized part of a tile: min(tile, page) tokens.
+    const int64_t page = int64_t(1) << paged->page_shift;
+    const int rows = static_cast<int>(page < var.tile_tokens ? page : var.tile_tokens);
+    if (paged->layout == ADB_PAGED_HND) {  // [blocks * kv_heads][page][D]
+      rc = kv_map(&tm_k, k, paged->num_blocks * s.Hkv, page, s.D, rows);
+      if (rc == ADB_OK) rc = kv_map(&tm_v, v, paged->num_blocks * s.Hkv, page, s.D, rows);
+    } else {  // [blocks][page][kv_heads][D]
+      rc = kv_map(&tm_k, k, paged->num_blocks, page, s.D, rows, 1, s.Hkv);
+      if (rc == ADB_OK) rc = kv_map(&tm_v, v, paged->num_blocks, page, s.D, rows, 1, s.Hkv);
+    }
+    if (rc != ADB_OK) return rc;
+  } else if (var.tma) {
     rc = kv_map(&tm_k, k, s.P, s.S, s.D, var.tile_tokens);
     if (rc != ADB_OK) return rc;
     rc = kv_map(&tm_v, v, s.P, s.S, s.D, var.tile_tokens);
@@ -429,6 +476,10 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
   p.steal = (allow_steal && var.tma && !deterministic_mode() && p.max_steals > 0) ? 1 : 0;
   p.dyn_capacity = plan.dyn_slots;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(s.D)));
+  p.block_table = paged != nullptr ? paged->block_table : nullptr;
+  p.bt_stride = paged != nullptr ? paged->bt_stride : 0;
+  p.paged = paged != nullptr ? (paged->layout == ADB_PAGED_HND ? 1 : 2) : 0;
+  p.page_shift = paged != nullptr ? paged->page_shift : 0;
   for (int r = 0; r < adb::kMaxRanks; ++r) p.x_base[r] = nullptr;
   p.x_world = 0;
   p.x_rank = 0;
@@ -551,6 +602,37 @@ int adb_decode_partial(const void* q, const void* k, const void* v, const int32_
     return fail(ADB_ERR_INVALID_ARGUMENT, "partial-state pointers must be non-null");
   return run_decode(q, k, v, seqlens, nullptr, acc, ml, batch, q_heads, kv_heads, kv_len, head_dim,
                     workspace, workspace_bytes, flags, device, stream);
+}
+
+int adb_decode_paged(const void* q, const void* k_cache, const void* v_cache,
+                     const int32_t* block_table, int64_t block_table_stride,
+                     const int32_t* seqlens, void* out, int64_t batch, int64_t q_heads,
+                     int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t page_size,
+                     int64_t max_blocks_per_seq, int layout, void* workspace,
+                     size_t workspace_bytes, unsigned flags, int device, void* stream) {
+  if (block_table == nullptr || seqlens == nullptr)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "paged decode needs a block table and sequence lengths");
+  if (layout != ADB_PAGED_HND && layout != ADB_PAGED_NHD)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "unknown paged layout %d (ADB_PAGED_HND or ADB_PAGED_NHD)",
+                layout);
+  if (page_size < 8 || page_size > (1 << 20) || (page_size & (page_size - 1)) != 0)
+    return fail(ADB_ERR_UNSUPPORTED, "page size must be a power of two from 8 to 2^20 (got %lld)",
+                (long long)page_size);
+  if (num_blocks <= 0 || max_blocks_per_seq <= 0)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "num_blocks and max_blocks_per_seq must be positive");
+  if (block_table_stride < max_blocks_per_seq)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "block table row stride %lld is below max_blocks_per_seq %lld",
+                (long long)block_table_stride, (long long)max_blocks_per_seq);
+  if (num_blocks * kv_heads > INT32_MAX)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "num_blocks * kv_heads exceeds 2^31-1");
+  int shift = 0;
+  while ((int64_t(1) << shift) < page_size) ++shift;
+  PagedArgs pa{block_table, block_table_stride, num_blocks, shift, layout};
+  // The sequence capacity (max_blocks_per_seq pages) plays the role of kv_len:
+  // lengths are clamped to it, and the workspace is sized for it.
+  return run_decode(q, k_cache, v_cache, seqlens, out, nullptr, nullptr, batch, q_heads, kv_heads,
+                    max_blocks_per_seq * page_size, head_dim, workspace, workspace_bytes, flags,
+                    device, stream, true, nullptr, &pa);
 }
 
 int adb_decode_no_alloc(const void* q, const void* k, const void* v, const int32_t* seqlens,

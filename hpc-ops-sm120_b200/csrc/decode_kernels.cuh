@@ -125,6 +125,15 @@ struct DecodeParams {
   int claim_divisor; // the last 1/claim_divisor of each range is claimable
   int64_t dyn_capacity;  // dynamic slots the workspace holds
   float scale_log2;  // log2(e) / sqrt(D)
+  // Paged K/V cache (paged != 0): K and V are pools of pages of 2^page_shift
+  // tokens, HND ([blocks][kv_heads][page][D], paged == 1) or NHD
+  // ([blocks][page][kv_heads][D], paged == 2); page j of sequence b is
+  // block_table[b * bt_stride + j].  A tile is loaded as TT / rows sub-boxes
+  // of rows = min(TT, page) tokens, each from its own page.
+  const int32_t* block_table;
+  int64_t bt_stride;
+  int paged;
+  int page_shift;
   // Peer exchange (kernel instantiated with kExchange): the partial states
   // go to slot x_rank of every rank's exchange buffer, not state_acc/ml.
   uint8_t* x_base[kMaxRanks];  // each rank's exchange buffer as mapped here
@@ -318,6 +327,8 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
                          const __grid_constant__ CUtensorMap tm_v, const DecodeParams p) {
   using C = StreamCfg<D, kWarps, kMB, kStages, kTma>;
   constexpr int TT = C::kTT;
+  constexpr int kTTShift = TT == 128 ? 7 : 6;
+  static_assert(TT == 64 || TT == 128, "tile tokens");
   constexpr int kSlabs = D / 16;
   constexpr int kCT = C::kConsumerThreads;
 
@@ -507,25 +518,74 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       const uint64_t policy = l2_policy_evict_first();
       int64_t k = 0;  // stage sequence number (lane 0)
       bool ok = true;
+      // Paged cache: tokens per sub-box and sub-boxes per tile.
+      constexpr int kMaxSub = TT / 8;
+      const int sub_shift = p.paged != 0 && p.page_shift < kTTShift ? p.page_shift : kTTShift;
+      const int n_sub = TT >> sub_shift;
       // Lane 0: fill stage k with `m` (and its tile, if it is one).
       auto issue = [&](const TileMeta& m) -> bool {
         const int s = static_cast<int>(k % kStages);
+        const bool is_tile = m.kind == kMetaOwn || m.kind == kMetaStolen;
+        // Paged: look the tile's pages up before waiting for the stage, so the
+        // block-table reads overlap the wait.  Sub-boxes past the sequence's
+        // last page reuse that page (their rows are masked as past the end).
+        int32_t blk[kMaxSub];
+        if (p.paged != 0 && is_tile) {
+          const int64_t tok0 = static_cast<int64_t>(m.tile_in_pair) * TT;
+          const int64_t last_page = m.len > 0 ? (static_cast<int64_t>(m.len) - 1) >> p.page_shift : 0;
+          const int32_t* row = p.block_table + static_cast<int64_t>(m.b) * p.bt_stride;
+#pragma unroll
+          for (int j = 0; j < kMaxSub; ++j) {
+            if (j < n_sub) {
+              int64_t pg = (tok0 + (static_cast<int64_t>(j) << sub_shift)) >> p.page_shift;
+              if (pg > last_page) pg = last_page;
+              blk[j] = __ldg(row + pg);
+            }
+          }
+        }
         if (k >= kStages &&
             !mbar_wait(empty_bar(s), static_cast<uint32_t>((k / kStages) - 1) & 1u, abort_flag))
           return false;
         meta[s] = m;
-        if (m.kind == kMetaOwn || m.kind == kMetaStolen) {
+        if (is_tile) {
           mbar_arrive_expect_tx(full_bar(s), C::kStageBytes);
           uint8_t* st = ring + static_cast<size_t>(s) * C::kStageBytes;
-          const int y = m.tile_in_pair * TT;
-          const int z = static_cast<int>(m.b * Hkv + m.h);
+          if (p.paged == 0) {
+            const int y = m.tile_in_pair * TT;
+            const int z = static_cast<int>(m.b * Hkv + m.h);
 #pragma unroll
-          for (int h = 0; h < C::kHalves; ++h)
-            tma_load_3d(smem_u32(st + h * C::kBoxBytes), &tm_k, h * 64, y, z, full_bar(s), policy);
+            for (int h = 0; h < C::kHalves; ++h)
+              tma_load_3d(smem_u32(st + h * C::kBoxBytes), &tm_k, h * 64, y, z, full_bar(s), policy);
 #pragma unroll
-          for (int h = 0; h < C::kHalves; ++h)
-            tma_load_3d(smem_u32(st + (C::kHalves + h) * C::kBoxBytes), &tm_v, h * 64, y, z,
-                        full_bar(s), policy);
+            for (int h = 0; h < C::kHalves; ++h)
+              tma_load_3d(smem_u32(st + (C::kHalves + h) * C::kBoxBytes), &tm_v, h * 64, y, z,
+                          full_bar(s), policy);
+          } else {
+            // Sub-box j lands at row j * rows of the stage's boxes; rows is a
+            // multiple of 8, so every sub-box starts on a 1024-byte swizzle
+            // atom and the layout equals one whole-tile load.
+            const int64_t tok0 = static_cast<int64_t>(m.tile_in_pair) * TT;
+            const int page_mask = (1 << p.page_shift) - 1;
+#pragma unroll
+            for (int j = 0; j < kMaxSub; ++j) {
+              if (j >= n_sub) break;
+              const int y = static_cast<int>((tok0 + (static_cast<int64_t>(j) << sub_shift)) & page_mask);
+              const uint32_t off = static_cast<uint32_t>(j << sub_shift) * 128u;
+#pragma unroll
+              for (int h = 0; h < C::kHalves; ++h) {
+                const uint32_t dk = smem_u32(st + h * C::kBoxBytes) + off;
+                const uint32_t dv = smem_u32(st + (C::kHalves + h) * C::kBoxBytes) + off;
+                if (p.paged == 1) {
+                  const int z = blk[j] * static_cast<int>(Hkv) + m.h;
+                  tma_load_3d(dk, &tm_k, h * 64, y, z, full_bar(s), policy);
+                  tma_load_3d(dv, &tm_v, h * 64, y, z, full_bar(s), policy);
+                } else {
+                  tma_load_4d(dk, &tm_k, h * 64, m.h, y, blk[j], full_bar(s), policy);
+                  tma_load_4d(dv, &tm_v, h * 64, m.h, y, blk[j], full_bar(s), policy);
+                }
+              }
+            }
+          }
         } else {
           mbar_arrive(full_bar(s));
         }

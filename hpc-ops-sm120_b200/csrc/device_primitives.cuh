@@ -101,6 +101,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// 4-D tiled bulk tensor load (paged caches laid out [blocks][page][heads][D]).
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            int z, int w, uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar), "l"(policy)
+      : "memory");
+}
+
 // L2 policy for data read once: evict it first (all of the access).
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t policy;

@@ -104,6 +104,30 @@ ADB_API int adb_decode(const void* q, const void* k, const void* v, const int32_
                        int64_t kv_len, int64_t head_dim, void* workspace,
                        size_t workspace_bytes, unsigned flags, int device, void* stream);
 
+/* Layouts of a paged K/V cache (adb_decode_paged). */
+#define ADB_PAGED_HND 0 /* [num_blocks][kv_heads][page_size][head_dim] */
+#define ADB_PAGED_NHD 1 /* [num_blocks][page_size][kv_heads][head_dim] */
+
+/* Decode over a paged K/V cache (no reference counterpart: the reference
+ * takes contiguous [B, Hkv, S, D] tensors only; this is the layout a serving
+ * engine's KV cache uses).  k_cache / v_cache are pools of num_blocks pages
+ * of page_size tokens each (bf16, 16-byte aligned, layout HND or NHD);
+ * page j of sequence b is block_table[b * block_table_stride + j] (int32 on
+ * the device), and sequence b uses its first seqlens[b] tokens (int32 on the
+ * device, clamped to [0, max_blocks_per_seq * page_size]).  page_size is a
+ * power of two from 8 to 2^20.  Only the pages that hold a sequence's tokens
+ * are read; block-table entries past a sequence's last page are never used.
+ * Size the workspace with adb_decode_workspace_size(batch, q_heads,
+ * kv_heads, max_blocks_per_seq * page_size, head_dim, 1, ...).  Output,
+ * flags, workspace and stream as adb_decode. */
+ADB_API int adb_decode_paged(const void* q, const void* k_cache, const void* v_cache,
+                             const int32_t* block_table, int64_t block_table_stride,
+                             const int32_t* seqlens, void* out, int64_t batch, int64_t q_heads,
+                             int64_t kv_heads, int64_t head_dim, int64_t num_blocks,
+                             int64_t page_size, int64_t max_blocks_per_seq, int layout,
+                             void* workspace, size_t workspace_bytes, unsigned flags, int device,
+                             void* stream);
+
 /* Size of the fixed device array that adb_decode_no_alloc uses as its
  * workspace (8 MiB, held by every GPU that loads the library). */
 #define ADB_NO_ALLOC_WORKSPACE_BYTES (8u << 20)

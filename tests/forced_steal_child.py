@@ -66,10 +66,28 @@ def run_case(index, name, batch, hq, hkv, length, dim, lengths, device):
     }
 
 
+def run_paged_case(device):
+    """A paged cache (16-token pages at shuffled block ids) with stealing on."""
+    from test_paged import make_paged
+
+    lengths = [30000, 5, 24000, 17, 9000, 31000]
+    q, k, v, kc, vc, table, lens = make_paged(device, lengths, 64, 8, 128, 16, "NHD", seed=4242)
+    expected = oracle_reference(q, k, v, lens).float()
+    worst_excess, finite = -1.0, True
+    for _ in range(REPEATS):
+        out = ad.attention_decode_paged(q, kc, vc, table, lens, layout="NHD").float()
+        finite &= bool(torch.isfinite(out).all().item())
+        worst_excess = max(worst_excess, ((out - expected).abs() - (ATOL + RTOL * expected.abs())).max().item())
+    torch.cuda.synchronize(device)
+    return {"case": "paged_nhd_p16", "finite": finite, "max_abs": None, "excess": worst_excess,
+            "partial_excess": -1.0, "error_flag": ad.read_error_flag(device.index or 0)}
+
+
 def main() -> int:
     device = torch.device("cuda", 0)
     for index, case in enumerate(CASES):
         print(json.dumps(run_case(index, *case, device=device)), flush=True)
+    print(json.dumps(run_paged_case(device)), flush=True)
     return 0
 
 

@@ -116,3 +116,15 @@ def test_exchange_arguments_are_checked_on_host():
     assert rc == _lib.ADB_ERR_INVALID_ARGUMENT
     rc = lib.adb_exchange_merge(256, 2, 64, 128, 512, 0, 0, None)
     assert rc == _lib.ADB_ERR_INVALID_ARGUMENT and "timeout" in _lib.last_error(lib)
+
+
+def test_paged_arguments_are_checked_on_host():
+    lib = _lib.load_library()
+    args = lambda page, layout, table=1: (  # noqa: E731
+        None, None, None, table, 4, 1, None, 2, 32, 8, 128, 16, page, 4, layout, None, 0, 0, 0, None)
+    assert lib.adb_decode_paged(*args(16, 0, table=None)) == _lib.ADB_ERR_INVALID_ARGUMENT
+    assert lib.adb_decode_paged(*args(16, 7)) == _lib.ADB_ERR_INVALID_ARGUMENT
+    assert "layout" in _lib.last_error(lib)
+    for page in (12, 4, 0, 3 << 20):
+        assert lib.adb_decode_paged(*args(page, 0)) == _lib.ADB_ERR_UNSUPPORTED
+        assert "power of two" in _lib.last_error(lib)
