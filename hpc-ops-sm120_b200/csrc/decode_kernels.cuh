@@ -64,6 +64,7 @@ constexpr int kMaxSteals = 16;          // most steals one thief CTA may make (s
 constexpr int kMaxTableBatches = 1024;  // varlen: per-batch tile table kept in shared memory
 constexpr int kStealChunk = 4;          // most tiles one steal takes
 constexpr int kStealMinRemaining = 4;   // a victim with fewer claimable tiles is left alone
+constexpr int kPrefetchTiles = 4;       // tiles warmed in L2 before the previous grid is done
 
 // ---------------------------------------------------------------- exchange
 // Sequence sharding over NVLink peer memory.  Every rank owns one exchange
@@ -375,6 +376,36 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       fence_barrier_init();
       prefetch_tensormap(&tm_k);
       prefetch_tensormap(&tm_v);
+    }
+  }
+  // While the previous grid in the stream drains, warm L2 with the first
+  // tiles this CTA will stream (uniform layout: the range follows from the
+  // parameters alone).  A prefetch reads nothing into the CTA and L2 is the
+  // coherence point, so later loads still see whatever the previous grid
+  // writes.  Long ranges (load balancing on) gain nothing from it.
+  if constexpr (kTma) {
+    if (warp == kWarps && lane == 0 && p.seqlens == nullptr && p.paged == 0 && !p.steal) {
+      const int64_t ntu = (S + TT - 1) / TT;
+      const int64_t ntt = P * ntu;
+      const int64_t a = c * ntt / nc, e = (c + 1) * ntt / nc, n = e - a;
+      if (n > 0) {
+        // processing order: the part of the last pair that continues into
+        // the next CTA's range first, then the range in order
+        const int64_t last_tile = (e - 1) % ntu;
+        int64_t rot = last_tile + 1 < ntu ? (last_tile + 1 < n ? last_tile + 1 : n) : 0;
+        if (rot == n) rot = 0;
+        const int64_t count = n < kPrefetchTiles ? n : kPrefetchTiles;
+        for (int64_t i = 0; i < count; ++i) {
+          const int64_t t = i < rot ? e - rot + i : a + i - rot;
+          const int y = static_cast<int>((t % ntu) * TT);
+          const int z = static_cast<int>(t / ntu);
+#pragma unroll
+          for (int h = 0; h < C::kHalves; ++h) {
+            tma_prefetch_3d(&tm_k, h * 64, y, z);
+            tma_prefetch_3d(&tm_v, h * 64, y, z);
+          }
+        }
+      }
     }
   }
   __syncthreads();

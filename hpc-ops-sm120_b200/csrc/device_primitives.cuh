@@ -111,6 +111,14 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Prefetch of one tiled box into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
 // L2 policy for data read once: evict it first (all of the access).
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t policy;
