@@ -64,7 +64,7 @@ constexpr int kMaxSteals = 16;          // most steals one thief CTA may make (s
 constexpr int kMaxTableBatches = 1024;  // varlen: per-batch tile table kept in shared memory
 constexpr int kStealChunk = 4;          // most tiles one steal takes
 constexpr int kStealMinRemaining = 4;   // a victim with fewer claimable tiles is left alone
-constexpr int kPrefetchTiles = 4;       // tiles warmed in L2 before the previous grid is done
+constexpr int kPrefetchTiles = 6;       // tiles warmed in L2 before the previous grid is done
 
 // ---------------------------------------------------------------- exchange
 // Sequence sharding over NVLink peer memory.  Every rank owns one exchange
