@@ -22,6 +22,7 @@ from ._lib import AttentionDecodeError
 
 __all__ = [
     "attention_decode",
+    "attention_decode_append",
     "attention_decode_paged",
     "attention_decode_partial",
     "combine_partials",
@@ -213,6 +214,50 @@ def attention_decode(q, k, v, seqlens=None):
     _validate(q, k, v, seqlens)
     out = _torch().empty_like(q)
     _launch(q, k, v, seqlens, out=out)
+    return out
+
+
+def attention_decode_append(q, k_new, v_new, k_cache, v_cache, seqlens):
+    """One decode step with this step's token appended (fuses the cache
+    append of a decode loop into the decode; the reference has no such step).
+
+    ``k_cache``/``v_cache`` [B,Hkv,S_cap,D] hold ``seqlens[b]`` tokens of
+    sequence b; ``k_new``/``v_new`` [B,Hkv,1,D] are the new token.  Returns
+    attention over the cached tokens and the new one (BF16 [B,Hq,1,D]) and
+    writes the new token into the caches at position ``seqlens[b]``.
+    ``seqlens`` is not modified: add one to it after the call.  A full cache
+    (``seqlens[b] >= S_cap``) is not written and sets bit 8 of
+    :func:`read_error_flag`.
+    """
+    torch = _torch()
+    if seqlens is None:
+        raise TypeError("attention_decode_append needs seqlens")
+    _validate(q, k_cache, v_cache, seqlens)
+    for name, t in (("k_new", k_new), ("v_new", v_new)):
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a tensor")
+        if not t.is_cuda or t.device != q.device:
+            raise ValueError(f"{name} must be a CUDA tensor on Q's device")
+        if t.dtype is not torch.bfloat16 or not t.is_contiguous():
+            _fail(f"{name} must be a contiguous BF16 tensor")
+        if tuple(t.shape) != (k_cache.shape[0], k_cache.shape[1], 1, k_cache.shape[3]):
+            _fail(f"{name} must have shape [batch, kv_heads, 1, head_dim]")
+    lib = _lib.load_library()
+    batch, q_heads, _, head_dim = q.shape
+    kv_heads, capacity = k_cache.shape[1], k_cache.shape[2]
+    device = q.device.index if q.device.index is not None else torch.cuda.current_device()
+    nbytes, header = workspace_bytes(batch, q_heads, kv_heads, capacity, head_dim, True, device)
+    stream = torch._C._cuda_getCurrentRawStream(device)
+    workspace, flags = _workspace(q.device, device, stream, nbytes, header)
+    out = torch.empty_like(q)
+    _lib.check(
+        lib,
+        lib.adb_decode_append(
+            q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+            seqlens.data_ptr(), out.data_ptr(), batch, q_heads, kv_heads, capacity, head_dim,
+            workspace.data_ptr(), workspace.numel(), flags, device, stream,
+        ),
+    )
     return out
 
 

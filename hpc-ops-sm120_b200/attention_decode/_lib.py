@@ -29,6 +29,7 @@ ADB_IPC_HANDLE_BYTES = 64
 ADB_PAGED_HND = 0
 ADB_PAGED_NHD = 1
 ADB_ERROR_FLAG_PEER_TIMEOUT = 4
+ADB_ERROR_FLAG_APPEND_FULL = 8
 
 STATUS_NAMES = {
     ADB_OK: "ok",
@@ -60,6 +61,10 @@ PROTOTYPES = {
     "adb_decode_partial": (
         _int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _size, _uint, _int, _vp],
+    ),
+    "adb_decode_append": (
+        _int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _size, _uint, _int, _vp],
     ),
     "adb_decode_paged": (
         _int,

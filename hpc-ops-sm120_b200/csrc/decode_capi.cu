@@ -59,6 +59,7 @@ struct Variant {
   bool tma;
   const void* fn;     // ordinary decode / partial decode
   const void* fn_x;   // partial decode into peer exchange buffers
+  const void* fn_a;   // decode with an appended token
 };
 
 template <int D, int W, int MB, int ST, bool TMA>
@@ -70,8 +71,9 @@ constexpr Variant make_variant(const char* name) {
                  C::kThreads,
                  C::kSmemBytes,
                  TMA,
-                 reinterpret_cast<const void*>(&adb::decode_stream_kernel<D, W, MB, ST, TMA, false>),
-                 reinterpret_cast<const void*>(&adb::decode_stream_kernel<D, W, MB, ST, TMA, true>)};
+                 reinterpret_cast<const void*>(&adb::decode_stream_kernel<D, W, MB, ST, TMA, adb::kModeDecode>),
+                 reinterpret_cast<const void*>(&adb::decode_stream_kernel<D, W, MB, ST, TMA, adb::kModeExchange>),
+                 reinterpret_cast<const void*>(&adb::decode_stream_kernel<D, W, MB, ST, TMA, adb::kModeAppend>)};
 }
 
 // Name format: d<head_dim>_<tma|generic>_tt<tile tokens>_s<stages>.
@@ -163,6 +165,8 @@ int prepare_variant(DeviceState* st, int vi) {
       cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem_bytes);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(v.fn_x, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem_bytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(v.fn_a, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem_bytes);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
   int blocks = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, v.fn, v.threads, v.smem_bytes);
@@ -382,6 +386,12 @@ struct PagedArgs {
   int layout;  // ADB_PAGED_HND or ADB_PAGED_NHD
 };
 
+// The new token of an appending decode (adb_decode_append): K/V rows [pairs][D].
+struct AppendArgs {
+  const void* k_new;
+  const void* v_new;
+};
+
 // Destinations of a decode whose partial states go to every rank's exchange
 // buffer (adb_decode_exchange).
 struct ExchangeArgs {
@@ -394,7 +404,8 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
                float* state_acc, float* state_ml, int64_t batch, int64_t q_heads, int64_t kv_heads,
                int64_t kv_len, int64_t head_dim, void* workspace, size_t workspace_bytes,
                unsigned flags, int device, void* stream_ptr, bool allow_steal = true,
-               const ExchangeArgs* exchange = nullptr, const PagedArgs* paged = nullptr) {
+               const ExchangeArgs* exchange = nullptr, const PagedArgs* paged = nullptr,
+               const AppendArgs* append = nullptr) {
   Shape s;
   int rc = check_shape(batch, q_heads, kv_heads, kv_len, head_dim, &s);
   if (rc != ADB_OK) return rc;
@@ -476,6 +487,10 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
   p.steal = (allow_steal && var.tma && !deterministic_mode() && p.max_steals > 0) ? 1 : 0;
   p.dyn_capacity = plan.dyn_slots;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(s.D)));
+  p.k_new = append != nullptr ? static_cast<const __nv_bfloat16*>(append->k_new) : nullptr;
+  p.v_new = append != nullptr ? static_cast<const __nv_bfloat16*>(append->v_new) : nullptr;
+  p.k_cache = append != nullptr ? static_cast<__nv_bfloat16*>(const_cast<void*>(k)) : nullptr;
+  p.v_cache = append != nullptr ? static_cast<__nv_bfloat16*>(const_cast<void*>(v)) : nullptr;
   p.block_table = paged != nullptr ? paged->block_table : nullptr;
   p.bt_stride = paged != nullptr ? paged->bt_stride : 0;
   p.paged = paged != nullptr ? (paged->layout == ADB_PAGED_HND ? 1 : 2) : 0;
@@ -515,7 +530,8 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   void* args[] = {&tm_k, &tm_v, &p};
-  cudaError_t e = cudaLaunchKernelExC(&cfg, exchange != nullptr ? var.fn_x : var.fn, args);
+  const void* fn = exchange != nullptr ? var.fn_x : (append != nullptr ? var.fn_a : var.fn);
+  cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
   if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   if (t_timing.enabled) {
@@ -602,6 +618,20 @@ int adb_decode_partial(const void* q, const void* k, const void* v, const int32_
     return fail(ADB_ERR_INVALID_ARGUMENT, "partial-state pointers must be non-null");
   return run_decode(q, k, v, seqlens, nullptr, acc, ml, batch, q_heads, kv_heads, kv_len, head_dim,
                     workspace, workspace_bytes, flags, device, stream);
+}
+
+int adb_decode_append(const void* q, const void* k_new, const void* v_new, void* k_cache,
+                      void* v_cache, const int32_t* seqlens, void* out, int64_t batch,
+                      int64_t q_heads, int64_t kv_heads, int64_t kv_capacity, int64_t head_dim,
+                      void* workspace, size_t workspace_bytes, unsigned flags, int device,
+                      void* stream) {
+  if (k_new == nullptr || v_new == nullptr || seqlens == nullptr)
+    return fail(ADB_ERR_INVALID_ARGUMENT,
+                "append needs the new token's K and V rows and the sequence lengths");
+  AppendArgs ap{k_new, v_new};
+  return run_decode(q, k_cache, v_cache, seqlens, out, nullptr, nullptr, batch, q_heads, kv_heads,
+                    kv_capacity, head_dim, workspace, workspace_bytes, flags, device, stream, true,
+                    nullptr, nullptr, &ap);
 }
 
 int adb_decode_paged(const void* q, const void* k_cache, const void* v_cache,

@@ -135,6 +135,13 @@ struct DecodeParams {
   int64_t bt_stride;
   int paged;
   int page_shift;
+  // Append (kModeAppend): the new token's K/V rows ([pairs][D]); they are
+  // folded into each output row and written into the cache (k_cache /
+  // v_cache, the same tensors as k / v) at position seqlens[b].
+  const __nv_bfloat16* k_new;
+  const __nv_bfloat16* v_new;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
   // Peer exchange (kernel instantiated with kExchange): the partial states
   // go to slot x_rank of every rank's exchange buffer, not state_acc/ml.
   uint8_t* x_base[kMaxRanks];  // each rank's exchange buffer as mapped here
@@ -320,13 +327,54 @@ __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-// kExchange: partial states go to every rank's exchange buffer (a separate
-// instantiation, so the per-rank stores cost the ordinary kernels nothing).
-template <int D, int kWarps, int kMB, int kStages, bool kTma, bool kExchange>
+// Appended token: score of query row `row` against the new key of `pair`
+// (log2 domain), one warp; every lane gets the sum.
+template <int D>
+__device__ __forceinline__ float append_score(const DecodeParams& p, int64_t row, int64_t pair,
+                                              int lane) {
+  constexpr int kPer = D / 32;
+  float dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i)
+    dot += __bfloat162float(p.q[row * D + lane * kPer + i]) *
+           __bfloat162float(p.k_new[pair * D + lane * kPer + i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+  return dot * p.scale_log2;
+}
+
+// Writes the new token's K and V rows into the cache at position `len` of
+// `pair` (threads tid, tid + nthreads, ...); a full cache gets no write and
+// sets the device error word.
+template <int D>
+__device__ __forceinline__ void append_store(const DecodeParams& p, int64_t pair, int32_t len,
+                                             int tid, int nthreads) {
+  if (len >= p.kv_len) {
+    if (tid == 0) atomicOr(&g_adb_error_flag, kErrAppendFull);
+    return;
+  }
+  const int64_t dst = (pair * p.kv_len + len) * D;
+  for (int d = tid; d < D; d += nthreads) {
+    p.k_cache[dst + d] = p.k_new[pair * D + d];
+    p.v_cache[dst + d] = p.v_new[pair * D + d];
+  }
+}
+
+// Kernel modes, each its own instantiation so that the extra work of one
+// costs the others nothing (registers and code of the shared paths):
+//   kModeDecode    decode / partial decode (local state arrays)
+//   kModeExchange  partial states go to every rank's exchange buffer
+//   kModeAppend    decode over the cache plus one new token, which is also
+//                  written into the cache
+constexpr int kModeDecode = 0, kModeExchange = 1, kModeAppend = 2;
+
+template <int D, int kWarps, int kMB, int kStages, bool kTma, int kMode>
 __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThreads, 1)
     decode_stream_kernel(const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const DecodeParams p) {
   using C = StreamCfg<D, kWarps, kMB, kStages, kTma>;
+  constexpr bool kExchange = kMode == kModeExchange;
+  constexpr bool kAppend = kMode == kModeAppend;
   constexpr int TT = C::kTT;
   constexpr int kTTShift = TT == 128 ? 7 : 6;
   static_assert(TT == 64 || TT == 128, "tile tokens");
@@ -488,6 +536,15 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       const int64_t Hq = Hkv * G;
       for (int64_t b = tid; b < B; b += blockDim.x) {
         if (clamped_len(p, b) != 0) continue;
+        if constexpr (kAppend) {  // only the new token: O = its V row, exactly
+          for (int64_t h = 0; h < Hkv; ++h) {
+            const int64_t pair = b * Hkv + h;
+            for (int64_t row = pair * G; row < (pair + 1) * G; ++row)
+              for (int d = 0; d < D; ++d) p.out[row * D + d] = p.v_new[pair * D + d];
+            append_store<D>(p, pair, 0, 0, 1);
+          }
+          continue;
+        }
         for (int64_t row = b * Hq; row < (b + 1) * Hq; ++row) {
           if (!p.partial_mode) {
             for (int d = 0; d < D; ++d) p.out[row * D + d] = __float2bfloat16_rn(0.f);
@@ -924,12 +981,23 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
             ml[2 * row + 1] = L;
           }
         }
+      } else if constexpr (kAppend) {
+        // fold the new token into the row: online-softmax update by one key
+        const float sn = append_score<D>(p, row, q, lane);
+        const float mn = fmaxf(mrun[hi], sn);
+        const float a = fast_exp2(mrun[hi] - mn), wn = fast_exp2(sn - mn);
+        const float La = L * a + wn;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i)
+          p.out[row * D + lane * kPer + i] = __float2bfloat16_rn(
+              (o[hi][i] * a + wn * __bfloat162float(p.v_new[q * D + lane * kPer + i])) / La);
       } else {
 #pragma unroll
         for (int i = 0; i < kPer; ++i)
           p.out[row * D + lane * kPer + i] = __float2bfloat16_rn(L > 0.f ? o[hi][i] / L : 0.f);
       }
     }
+    if constexpr (kAppend) append_store<D>(p, q, clamped_len(p, q / Hkv), tid, kCT);
   };
 
   // Commit `add` for pair q (after this CTA's segment of q is written) and
@@ -1017,6 +1085,16 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       reset_state();
       return;
     }
+    if constexpr (kAppend) {
+      // new-token scores of the pair's heads, for the output below
+      if (complete) {
+        for (int hd = warp; hd < G; hd += kWarps) {
+          const float sn = append_score<D>(p, pair * G + hd, pair, lane);
+          if (lane == 0) misc[56 + hd] = __float_as_int(sn);
+        }
+        bar();
+      }
+    }
     for (int e = tid; e < G * D; e += kCT) {
       const int hd = e / D, d = e - hd * D;
       float M = neg_inf();
@@ -1031,7 +1109,13 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
         O += f * fl_acc[(ww * kMaxGroup + hd) * D + d];
       }
       const int64_t row = pair * G + hd;
-      if (complete && !p.partial_mode) {
+      if (kAppend && complete) {
+        const float sn = __int_as_float(static_cast<int>(misc[56 + hd]));
+        const float mn = fmaxf(M, sn);
+        const float a = fast_exp2(M - mn), wn = fast_exp2(sn - mn);
+        p.out[row * D + d] = __float2bfloat16_rn(
+            (O * a + wn * __bfloat162float(p.v_new[pair * D + d])) / (L * a + wn));
+      } else if (complete && !p.partial_mode) {
         p.out[row * D + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
       } else if (complete) {
         for (int s = 0; s < partial_copies<kExchange>(p); ++s) {
@@ -1050,6 +1134,9 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
           p.ws_ml[2 * srow + 1] = L;
         }
       }
+    }
+    if constexpr (kAppend) {
+      if (complete) append_store<D>(p, pair, clamped_len(p, pair / Hkv), tid, kCT);
     }
     bar();  // fl_* reads done before the merge scratch (aliased) is used
     if (!complete)

@@ -62,6 +62,7 @@ __device__ int g_adb_error_flag = 0;
 constexpr int kErrWaitTimeout = 1;
 constexpr int kErrWorkspace = 2;  // a scheduler counter left its bounds (dirty header)
 constexpr int kErrPeerTimeout = 4;  // a peer's partial states did not arrive in time
+constexpr int kErrAppendFull = 8;   // append: a sequence's cache had no free position
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far above any legitimate wait
 
 // Waits for the given phase parity of an mbarrier.  The wait is bounded: if

@@ -104,6 +104,27 @@ ADB_API int adb_decode(const void* q, const void* k, const void* v, const int32_
                        int64_t kv_len, int64_t head_dim, void* workspace,
                        size_t workspace_bytes, unsigned flags, int device, void* stream);
 
+/* One decode step of a serving loop with the new token appended (no
+ * reference counterpart: the reference decodes a cache that already holds
+ * every token).  Sequence b has seqlens[b] tokens cached in k_cache /
+ * v_cache [batch, kv_heads, kv_capacity, head_dim] (bf16, contiguous); the
+ * step's new token is k_new / v_new [batch, kv_heads, 1, head_dim].  The
+ * output is attention over the seqlens[b] cached tokens and the new one --
+ * what adb_decode computes after the token is written at position
+ * seqlens[b] and the length raised by one -- and the kernel also writes the
+ * new token into the cache at position seqlens[b], replacing the separate
+ * append launch of a decode loop.  seqlens is not modified (raise it on the
+ * stream after the call).  A sequence whose cache is full (seqlens[b] >=
+ * kv_capacity) gets attention over kv_capacity cached tokens and the new
+ * one, no write, and bit 8 of the device error word (adb_read_error_flag).
+ * Workspace as adb_decode with kv_len = kv_capacity and has_seqlens = 1. */
+#define ADB_ERROR_FLAG_APPEND_FULL 8
+ADB_API int adb_decode_append(const void* q, const void* k_new, const void* v_new, void* k_cache,
+                              void* v_cache, const int32_t* seqlens, void* out, int64_t batch,
+                              int64_t q_heads, int64_t kv_heads, int64_t kv_capacity,
+                              int64_t head_dim, void* workspace, size_t workspace_bytes,
+                              unsigned flags, int device, void* stream);
+
 /* Layouts of a paged K/V cache (adb_decode_paged). */
 #define ADB_PAGED_HND 0 /* [num_blocks][kv_heads][page_size][head_dim] */
 #define ADB_PAGED_NHD 1 /* [num_blocks][page_size][kv_heads][head_dim] */

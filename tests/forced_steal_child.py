@@ -83,11 +83,33 @@ def run_paged_case(device):
             "partial_excess": -1.0, "error_flag": ad.read_error_flag(device.index or 0)}
 
 
+def run_append_case(device):
+    """Decode with an appended token, stealing on: output and cache write."""
+    lengths = [20000, 3, 16000, 0, 12000]
+    batch, hkv, cap, dim = len(lengths), 8, 20480, 128
+    q, k, v = inputs(device, cap, dim, hkv, batch=batch, hq=64, seed=4343)
+    k_new = k[:, :, :1].flip(0).contiguous()
+    v_new = v[:, :, :1].flip(0).contiguous()
+    lens = torch.tensor(lengths, dtype=torch.int32, device=device)
+    k2, v2 = k.clone(), v.clone()
+    for b, n in enumerate(lengths):
+        k2[b, :, n] = k_new[b, :, 0]
+        v2[b, :, n] = v_new[b, :, 0]
+    expected = oracle_reference(q, k2, v2, lens + 1).float()
+    out = ad.attention_decode_append(q, k_new, v_new, k, v, lens).float()
+    torch.cuda.synchronize(device)
+    excess = ((out - expected).abs() - (ATOL + RTOL * expected.abs())).max().item()
+    cache_ok = bool(torch.equal(k, k2) and torch.equal(v, v2))
+    return {"case": "append", "finite": bool(torch.isfinite(out).all().item()) and cache_ok, "max_abs": None,
+            "excess": excess, "partial_excess": -1.0, "error_flag": ad.read_error_flag(device.index or 0)}
+
+
 def main() -> int:
     device = torch.device("cuda", 0)
     for index, case in enumerate(CASES):
         print(json.dumps(run_case(index, *case, device=device)), flush=True)
     print(json.dumps(run_paged_case(device)), flush=True)
+    print(json.dumps(run_append_case(device)), flush=True)
     return 0
 
 

@@ -128,3 +128,9 @@ def test_paged_arguments_are_checked_on_host():
     for page in (12, 4, 0, 3 << 20):
         assert lib.adb_decode_paged(*args(page, 0)) == _lib.ADB_ERR_UNSUPPORTED
         assert "power of two" in _lib.last_error(lib)
+
+
+def test_append_arguments_are_checked_on_host():
+    lib = _lib.load_library()
+    rc = lib.adb_decode_append(None, None, None, None, None, None, None, 1, 32, 8, 128, 128, None, 0, 0, 0, None)
+    assert rc == _lib.ADB_ERR_INVALID_ARGUMENT and "append" in _lib.last_error(lib)

@@ -30,7 +30,7 @@ def test_forced_stealing_matches_oracle(claim_divisor, device):
     )
     assert proc.returncode == 0, proc.stderr[-4000:]
     results = [json.loads(line) for line in proc.stdout.splitlines() if line.startswith("{")]
-    assert len(results) == 6, proc.stdout
+    assert len(results) == 7, proc.stdout
     for r in results:
         assert r["finite"], r
         assert r["excess"] <= 0.0, r
