@@ -23,6 +23,7 @@ from ._lib import AttentionDecodeError
 __all__ = [
     "attention_decode",
     "attention_decode_append",
+    "attention_decode_fp8",
     "attention_decode_paged",
     "attention_decode_partial",
     "combine_partials",
@@ -214,6 +215,58 @@ def attention_decode(q, k, v, seqlens=None):
     _validate(q, k, v, seqlens)
     out = _torch().empty_like(q)
     _launch(q, k, v, seqlens, out=out)
+    return out
+
+
+def attention_decode_fp8(q, k, v, seqlens=None, *, k_scale=1.0, v_scale=1.0):
+    """Decode over an FP8 (``torch.float8_e4m3fn``) K/V cache that stands for
+    ``k * k_scale`` and ``v * v_scale`` (per-tensor scales).  Q is BF16
+    [B,Hq,1,128]; K/V are [B,Hkv,S,128] e4m3.  Half the bytes of the BF16
+    path; the reference reads BF16 only.  Returns BF16 [B,Hq,1,128].
+    """
+    torch = _torch()
+    Tensor = torch.Tensor
+    if not (isinstance(q, Tensor) and isinstance(k, Tensor) and isinstance(v, Tensor)):
+        raise TypeError("Q, K, and V must be tensors")
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise ValueError("Q, K, and V must be CUDA tensors")
+    if q.dtype is not torch.bfloat16:
+        _fail("Q dtype must be BF16 (bfloat16)")
+    if k.dtype is not torch.float8_e4m3fn or v.dtype is not torch.float8_e4m3fn:
+        _fail("K/V dtype must be float8_e4m3fn")
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        _fail("Q/K/V must have rank four")
+    if not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
+        _fail("Q/K/V must be contiguous")
+    if q.device != k.device or q.device != v.device:
+        _fail("Q/K/V device must match")
+    if k.shape != v.shape:
+        _fail("K/V shape must match")
+    if q.shape[2] != 1:
+        _fail("query length must be 1")
+    if q.shape[0] != k.shape[0] or q.shape[3] != k.shape[3]:
+        _fail("Q/K/V batch and head dimension must match")
+    if q.shape[1] % k.shape[1] != 0:
+        _fail("query heads must be divisible by KV heads")
+    if seqlens is not None and (seqlens.dtype != torch.int32 or seqlens.dim() != 1
+                                or seqlens.shape[0] != q.shape[0] or seqlens.device != q.device):
+        _fail("seqlens must be an int32 [batch] tensor on Q's device")
+    lib = _lib.load_library()
+    batch, q_heads, _, head_dim = q.shape
+    kv_heads, kv_len = k.shape[1], k.shape[2]
+    device = q.device.index if q.device.index is not None else torch.cuda.current_device()
+    nbytes, header = workspace_bytes(batch, q_heads, kv_heads, kv_len, head_dim, seqlens is not None, device)
+    stream = torch._C._cuda_getCurrentRawStream(device)
+    workspace, flags = _workspace(q.device, device, stream, nbytes, header)
+    out = torch.empty_like(q)
+    _lib.check(
+        lib,
+        lib.adb_decode_fp8(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), seqlens.data_ptr() if seqlens is not None else None,
+            out.data_ptr(), batch, q_heads, kv_heads, kv_len, head_dim, float(k_scale), float(v_scale),
+            workspace.data_ptr(), workspace.numel(), flags, device, stream,
+        ),
+    )
     return out
 
 

@@ -62,6 +62,11 @@ PROTOTYPES = {
         _int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _size, _uint, _int, _vp],
     ),
+    "adb_decode_fp8": (
+        _int,
+        [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, ctypes.c_float,
+         _vp, _size, _uint, _int, _vp],
+    ),
     "adb_decode_append": (
         _int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _size, _uint, _int, _vp],

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -60,6 +61,7 @@ struct Variant {
   const void* fn;     // ordinary decode / partial decode
   const void* fn_x;   // partial decode into peer exchange buffers
   const void* fn_a;   // decode with an appended token
+  bool fp8;           // K/V are e4m3 (fn only)
 };
 
 template <int D, int W, int MB, int ST, bool TMA>
@@ -73,7 +75,16 @@ constexpr Variant make_variant(const char* name) {
                  TMA,
                  reinterpret_cast<const void*>(&adb::decode_stream_kernel<D, W, MB, ST, TMA, adb::kModeDecode>),
                  reinterpret_cast<const void*>(&adb::decode_stream_kernel<D, W, MB, ST, TMA, adb::kModeExchange>),
-                 reinterpret_cast<const void*>(&adb::decode_stream_kernel<D, W, MB, ST, TMA, adb::kModeAppend>)};
+                 reinterpret_cast<const void*>(&adb::decode_stream_kernel<D, W, MB, ST, TMA, adb::kModeAppend>),
+                 false};
+}
+
+template <int W, int MB, int ST>
+constexpr Variant make_fp8_variant(const char* name) {
+  using C = adb::StreamCfg<128, W, MB, ST, true, 1>;
+  return Variant{name, 128, C::kTT, C::kThreads, C::kSmemBytes, true,
+                 reinterpret_cast<const void*>(&adb::decode_stream_kernel<128, W, MB, ST, true, adb::kModeFp8>),
+                 nullptr, nullptr, true};
 }
 
 // Name format: d<head_dim>_<tma|generic>_tt<tile tokens>_s<stages>.
@@ -85,10 +96,13 @@ const Variant kVariants[] = {
     make_variant<64, 4, 1, 6, true>("d64_tma_tt64_s6"),
     make_variant<128, 4, 1, 1, false>("d128_generic_tt64"),
     make_variant<64, 4, 1, 1, false>("d64_generic_tt64"),
+    make_fp8_variant<4, 2, 6>("d128_fp8_tt128_s6"),
+    make_fp8_variant<4, 1, 8>("d128_fp8_tt64_s8"),
+    make_fp8_variant<8, 1, 5>("d128_fp8_w8_tt128_s5"),
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 constexpr int kDefaultTma128 = 0, kSmallTma128 = 1, kDefaultTma64 = 3, kSmallTma64 = 4;
-constexpr int kGeneric128 = 5, kGeneric64 = 6;
+constexpr int kGeneric128 = 5, kGeneric64 = 6, kDefaultFp8 = 9, kSmallFp8 = 8;
 
 // ------------------------------------------------------------ device cache
 struct DeviceState {
@@ -163,9 +177,9 @@ int prepare_variant(DeviceState* st, int vi) {
   const Variant& v = kVariants[vi];
   cudaError_t e =
       cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem_bytes);
-  if (e == cudaSuccess)
+  if (e == cudaSuccess && v.fn_x != nullptr)
     e = cudaFuncSetAttribute(v.fn_x, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem_bytes);
-  if (e == cudaSuccess)
+  if (e == cudaSuccess && v.fn_a != nullptr)
     e = cudaFuncSetAttribute(v.fn_a, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem_bytes);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
   int blocks = 0;
@@ -203,16 +217,20 @@ int get_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) {
 // 64 columns (128 bytes, swizzled) x tile_tokens rows x 1 pair.  Rows past S
 // are outside the tensor and read as zeros.
 int encode_kv_map(CUtensorMap* map, const void* base, int64_t pairs, int64_t S, int64_t D,
-                  int tile_tokens) {
+                  int tile_tokens, int elem_bytes = 2) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   int rc = get_encoder(&encode);
   if (rc != ADB_OK) return rc;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S),
                         static_cast<cuuint64_t>(pairs)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(S * D * 2)};
-  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(tile_tokens), 1u};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * elem_bytes),
+                           static_cast<cuuint64_t>(S * D * elem_bytes)};
+  // one box row is 128 bytes (the swizzle span): 64 bf16 or 128 e4m3 values
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / elem_bytes), static_cast<cuuint32_t>(tile_tokens), 1u};
   cuuint32_t elem[3] = {1u, 1u, 1u};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+  const CUtensorMapDataType dtype =
+      elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = encode(map, dtype, 3, const_cast<void*>(base), dims,
                       strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(ADB_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
@@ -246,7 +264,7 @@ struct MapCacheEntry {
   const void* base = nullptr;
   int64_t pairs = 0, S = 0, D = 0, heads = 0;
   int tile_tokens = 0;
-  int layout = 0;  // 0: 3-D [rows][S][D]; 1: 4-D NHD pages (pairs = blocks, S = page)
+  int layout = 0;  // 0: 3-D [rows][S][D] bf16; 1: 4-D NHD pages (pairs = blocks, S = page); 2: 3-D e4m3
   CUtensorMap map;
 };
 constexpr int kMapCacheEntries = 8;
@@ -261,8 +279,9 @@ int kv_map(CUtensorMap* map, const void* base, int64_t pairs, int64_t S, int64_t
       *map = e.map;
       return ADB_OK;
     }
-  const int rc = layout == 0 ? encode_kv_map(map, base, pairs, S, D, tile_tokens)
-                             : encode_nhd_map(map, base, pairs, S, heads, D, tile_tokens);
+  const int rc = layout == 0   ? encode_kv_map(map, base, pairs, S, D, tile_tokens)
+                 : layout == 2 ? encode_kv_map(map, base, pairs, S, D, tile_tokens, 1)
+                               : encode_nhd_map(map, base, pairs, S, heads, D, tile_tokens);
   if (rc != ADB_OK) return rc;
   MapCacheEntry& e = t_map_cache[t_map_cache_next];
   t_map_cache_next = (t_map_cache_next + 1) % kMapCacheEntries;
@@ -322,20 +341,22 @@ struct Plan {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-int choose_variant(const Shape& s, bool tma) {
-  if (!tma) return s.D == 128 ? kGeneric128 : kGeneric64;
+int choose_variant(const Shape& s, bool tma, bool fp8 = false) {
   const int forced = forced_variant();
-  if (forced >= 0 && kVariants[forced].head_dim == s.D && kVariants[forced].tma) return forced;
+  if (fp8) return forced >= 0 && kVariants[forced].fp8 ? forced : kDefaultFp8;
+  if (!tma) return s.D == 128 ? kGeneric128 : kGeneric64;
+  if (forced >= 0 && kVariants[forced].head_dim == s.D && kVariants[forced].tma && !kVariants[forced].fp8)
+    return forced;
   return s.D == 128 ? kDefaultTma128 : kDefaultTma64;
 }
 
 int make_plan(const Shape& s, bool varlen, bool tma, DeviceState* st, Plan* plan,
-              bool allow_steal = true) {
-  int vi = choose_variant(s, tma);
+              bool allow_steal = true, bool fp8 = false) {
+  int vi = choose_variant(s, tma, fp8);
   // Small problems: prefer the 64-token tile so more SMs get work.
   if (tma && forced_variant() < 0) {
     const int64_t tiles = s.P * ((s.S + kVariants[vi].tile_tokens - 1) / kVariants[vi].tile_tokens);
-    if (tiles < 2LL * st->sms) vi = s.D == 128 ? kSmallTma128 : kSmallTma64;
+    if (tiles < 2LL * st->sms) vi = fp8 ? kSmallFp8 : (s.D == 128 ? kSmallTma128 : kSmallTma64);
   }
   int rc = prepare_variant(st, vi);
   if (rc != ADB_OK) return rc;
@@ -386,6 +407,12 @@ struct PagedArgs {
   int layout;  // ADB_PAGED_HND or ADB_PAGED_NHD
 };
 
+// Dequantisation scales of an e4m3 K/V cache (adb_decode_fp8).
+struct Fp8Args {
+  float k_scale;
+  float v_scale;
+};
+
 // The new token of an appending decode (adb_decode_append): K/V rows [pairs][D].
 struct AppendArgs {
   const void* k_new;
@@ -405,7 +432,7 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
                int64_t kv_len, int64_t head_dim, void* workspace, size_t workspace_bytes,
                unsigned flags, int device, void* stream_ptr, bool allow_steal = true,
                const ExchangeArgs* exchange = nullptr, const PagedArgs* paged = nullptr,
-               const AppendArgs* append = nullptr) {
+               const AppendArgs* append = nullptr, const Fp8Args* fp8 = nullptr) {
   Shape s;
   int rc = check_shape(batch, q_heads, kv_heads, kv_len, head_dim, &s);
   if (rc != ADB_OK) return rc;
@@ -423,8 +450,13 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
   const bool tma = is_aligned(k, 16) && is_aligned(v, 16);
   if (paged != nullptr && !tma)
     return fail(ADB_ERR_INVALID_ARGUMENT, "paged K/V caches must be 16-byte aligned");
+  if (fp8 != nullptr && !tma)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "FP8 K/V caches must be 16-byte aligned");
+  if (fp8 != nullptr && s.D != 128)
+    return fail(ADB_ERR_UNSUPPORTED, "FP8 K/V supports head dimension 128 only (got %lld)",
+                (long long)s.D);
   Plan plan;
-  rc = make_plan(s, seqlens != nullptr, tma, st, &plan, allow_steal);
+  rc = make_plan(s, seqlens != nullptr, tma, st, &plan, allow_steal, fp8 != nullptr);
   if (rc != ADB_OK) return rc;
   if (workspace == nullptr || !is_aligned(workspace, 256))
     return fail(ADB_ERR_WORKSPACE, "workspace must be a non-null 256-byte aligned device buffer");
@@ -449,9 +481,10 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
     }
     if (rc != ADB_OK) return rc;
   } else if (var.tma) {
-    rc = kv_map(&tm_k, k, s.P, s.S, s.D, var.tile_tokens);
+    const int layout = var.fp8 ? 2 : 0;
+    rc = kv_map(&tm_k, k, s.P, s.S, s.D, var.tile_tokens, layout);
     if (rc != ADB_OK) return rc;
-    rc = kv_map(&tm_v, v, s.P, s.S, s.D, var.tile_tokens);
+    rc = kv_map(&tm_v, v, s.P, s.S, s.D, var.tile_tokens, layout);
     if (rc != ADB_OK) return rc;
   }
 
@@ -486,7 +519,11 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
   p.claim_divisor = claim_divisor >= 2 ? claim_divisor : 2;
   p.steal = (allow_steal && var.tma && !deterministic_mode() && p.max_steals > 0) ? 1 : 0;
   p.dyn_capacity = plan.dyn_slots;
-  p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(s.D)));
+  // The FP8 kernel's f16 operands hold e4m3 values times 2^-8: 2^8 goes into
+  // both scales.
+  p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(s.D)) *
+                                    (fp8 != nullptr ? 256.0 * static_cast<double>(fp8->k_scale) : 1.0));
+  p.v_scale = fp8 != nullptr ? 256.f * fp8->v_scale : 1.f;
   p.k_new = append != nullptr ? static_cast<const __nv_bfloat16*>(append->k_new) : nullptr;
   p.v_new = append != nullptr ? static_cast<const __nv_bfloat16*>(append->v_new) : nullptr;
   p.k_cache = append != nullptr ? static_cast<__nv_bfloat16*>(const_cast<void*>(k)) : nullptr;
@@ -593,13 +630,18 @@ int adb_decode_workspace_size(int64_t batch, int64_t q_heads, int64_t kv_heads, 
   DeviceState* st = nullptr;
   rc = probe_device(device, &st);
   if (rc != ADB_OK) return rc;
-  Plan a, b;
+  Plan a, b, f;
   rc = make_plan(s, has_seqlens != 0, true, st, &a);
   if (rc != ADB_OK) return rc;
   rc = make_plan(s, has_seqlens != 0, false, st, &b);
   if (rc != ADB_OK) return rc;
-  *bytes = a.bytes > b.bytes ? a.bytes : b.bytes;
-  if (header_bytes != nullptr) *header_bytes = a.header_bytes > b.header_bytes ? a.header_bytes : b.header_bytes;
+  f = a;
+  if (s.D == 128) {  // the FP8 kernels (adb_decode_fp8) may plan differently
+    rc = make_plan(s, has_seqlens != 0, true, st, &f, true, true);
+    if (rc != ADB_OK) return rc;
+  }
+  *bytes = std::max({a.bytes, b.bytes, f.bytes});
+  if (header_bytes != nullptr) *header_bytes = std::max({a.header_bytes, b.header_bytes, f.header_bytes});
   return ADB_OK;
 }
 
@@ -618,6 +660,18 @@ int adb_decode_partial(const void* q, const void* k, const void* v, const int32_
     return fail(ADB_ERR_INVALID_ARGUMENT, "partial-state pointers must be non-null");
   return run_decode(q, k, v, seqlens, nullptr, acc, ml, batch, q_heads, kv_heads, kv_len, head_dim,
                     workspace, workspace_bytes, flags, device, stream);
+}
+
+int adb_decode_fp8(const void* q, const void* k, const void* v, const int32_t* seqlens, void* out,
+                   int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t kv_len,
+                   int64_t head_dim, float k_scale, float v_scale, void* workspace,
+                   size_t workspace_bytes, unsigned flags, int device, void* stream) {
+  if (!(k_scale > 0.f) || !(v_scale > 0.f) || !std::isfinite(k_scale) || !std::isfinite(v_scale))
+    return fail(ADB_ERR_INVALID_ARGUMENT, "FP8 scales must be positive and finite");
+  Fp8Args fa{k_scale, v_scale};
+  return run_decode(q, k, v, seqlens, out, nullptr, nullptr, batch, q_heads, kv_heads, kv_len,
+                    head_dim, workspace, workspace_bytes, flags, device, stream, true, nullptr,
+                    nullptr, nullptr, &fa);
 }
 
 int adb_decode_append(const void* q, const void* k_new, const void* v_new, void* k_cache,

@@ -142,6 +142,9 @@ struct DecodeParams {
   const __nv_bfloat16* v_new;
   __nv_bfloat16* k_cache;
   __nv_bfloat16* v_cache;
+  // FP8 K/V (kModeFp8): V's dequantisation scale, applied to every output
+  // (K's is folded into scale_log2).
+  float v_scale;
   // Peer exchange (kernel instantiated with kExchange): the partial states
   // go to slot x_rank of every rank's exchange buffer, not state_acc/ml.
   uint8_t* x_base[kMaxRanks];  // each rank's exchange buffer as mapped here
@@ -294,10 +297,11 @@ __device__ __forceinline__ TileMeta meta_marker(int32_t kind) {
   return m;
 }
 
-template <int D, int kWarps, int kMB, int kStages, bool kTma>
+template <int D, int kWarps, int kMB, int kStages, bool kTma, int kElem = 2>
 struct StreamCfg {
   static constexpr int kTT = 16 * kWarps * kMB;  // tokens per tile
-  static constexpr int kHalves = D / 64;         // 64-column (128-byte) swizzle atoms per row
+  static constexpr int kHalves = D * kElem / 128;  // 128-byte swizzle atoms per K/V row
+  static constexpr int kBoxCols = 128 / kElem;     // elements per box row
   static constexpr int kBoxBytes = kTT * 128;    // one TMA box: kTT rows x 128 B
   static constexpr int kStageBytes = 2 * kHalves * kBoxBytes;  // K and V
   static constexpr int kRingStages = kTma ? kStages : 1;
@@ -366,15 +370,18 @@ __device__ __forceinline__ void append_store(const DecodeParams& p, int64_t pair
 //   kModeExchange  partial states go to every rank's exchange buffer
 //   kModeAppend    decode over the cache plus one new token, which is also
 //                  written into the cache
-constexpr int kModeDecode = 0, kModeExchange = 1, kModeAppend = 2;
+//   kModeFp8       decode / partial decode of an FP8 (e4m3) K/V cache
+constexpr int kModeDecode = 0, kModeExchange = 1, kModeAppend = 2, kModeFp8 = 3;
 
 template <int D, int kWarps, int kMB, int kStages, bool kTma, int kMode>
 __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThreads, 1)
     decode_stream_kernel(const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const DecodeParams p) {
-  using C = StreamCfg<D, kWarps, kMB, kStages, kTma>;
+  constexpr bool kFp8 = kMode == kModeFp8;
+  using C = StreamCfg<D, kWarps, kMB, kStages, kTma, kFp8 ? 1 : 2>;
   constexpr bool kExchange = kMode == kModeExchange;
   constexpr bool kAppend = kMode == kModeAppend;
+  static_assert(!kFp8 || (D == 128 && kTma), "FP8 K/V: head_dim 128, TMA path");
   constexpr int TT = C::kTT;
   constexpr int kTTShift = TT == 128 ? 7 : 6;
   static_assert(TT == 64 || TT == 128, "tile tokens");
@@ -449,8 +456,8 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
           const int z = static_cast<int>(t / ntu);
 #pragma unroll
           for (int h = 0; h < C::kHalves; ++h) {
-            tma_prefetch_3d(&tm_k, h * 64, y, z);
-            tma_prefetch_3d(&tm_v, h * 64, y, z);
+            tma_prefetch_3d(&tm_k, h * C::kBoxCols, y, z);
+            tma_prefetch_3d(&tm_v, h * C::kBoxCols, y, z);
           }
         }
       }
@@ -643,10 +650,10 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
             const int z = static_cast<int>(m.b * Hkv + m.h);
 #pragma unroll
             for (int h = 0; h < C::kHalves; ++h)
-              tma_load_3d(smem_u32(st + h * C::kBoxBytes), &tm_k, h * 64, y, z, full_bar(s), policy);
+              tma_load_3d(smem_u32(st + h * C::kBoxBytes), &tm_k, h * C::kBoxCols, y, z, full_bar(s), policy);
 #pragma unroll
             for (int h = 0; h < C::kHalves; ++h)
-              tma_load_3d(smem_u32(st + (C::kHalves + h) * C::kBoxBytes), &tm_v, h * 64, y, z,
+              tma_load_3d(smem_u32(st + (C::kHalves + h) * C::kBoxBytes), &tm_v, h * C::kBoxCols, y, z,
                           full_bar(s), policy);
           } else {
             // Sub-box j lands at row j * rows of the stage's boxes; rows is a
@@ -665,11 +672,11 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
                 const uint32_t dv = smem_u32(st + (C::kHalves + h) * C::kBoxBytes) + off;
                 if (p.paged == 1) {
                   const int z = blk[j] * static_cast<int>(Hkv) + m.h;
-                  tma_load_3d(dk, &tm_k, h * 64, y, z, full_bar(s), policy);
-                  tma_load_3d(dv, &tm_v, h * 64, y, z, full_bar(s), policy);
+                  tma_load_3d(dk, &tm_k, h * C::kBoxCols, y, z, full_bar(s), policy);
+                  tma_load_3d(dv, &tm_v, h * C::kBoxCols, y, z, full_bar(s), policy);
                 } else {
-                  tma_load_4d(dk, &tm_k, h * 64, m.h, y, blk[j], full_bar(s), policy);
-                  tma_load_4d(dv, &tm_v, h * 64, m.h, y, blk[j], full_bar(s), policy);
+                  tma_load_4d(dk, &tm_k, h * C::kBoxCols, m.h, y, blk[j], full_bar(s), policy);
+                  tma_load_4d(dv, &tm_v, h * C::kBoxCols, m.h, y, blk[j], full_bar(s), policy);
                 }
               }
             }
@@ -809,9 +816,21 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       const uint16_t* row = q16 + (pair * G + g) * D;
 #pragma unroll
       for (int j = 0; j < kSlabs; ++j) {
-        qf[j][0] = pack_u16x2(__ldg(row + 16 * j + 2 * t), __ldg(row + 16 * j + 2 * t + 1));
-        qf[j][1] =
-            pack_u16x2(__ldg(row + 16 * j + 8 + 2 * t), __ldg(row + 16 * j + 8 + 2 * t + 1));
+        if constexpr (kFp8) {
+          // f16, reduction index k of slab j = dims 16j + {4t, 4t+1} (k = 2t,
+          // 2t+1) and 16j + {4t+2, 4t+3} (k = 2t+8, 2t+9): the order in which
+          // a 16-bit ldmatrix delivers the FP8 K row (the dot product is the
+          // same under any common permutation of its index)
+          const uint16_t* r4 = row + 16 * j + 4 * t;
+          qf[j][0] = pack_f16x2(__bfloat162float(__ushort_as_bfloat16(__ldg(r4))),
+                                __bfloat162float(__ushort_as_bfloat16(__ldg(r4 + 1))));
+          qf[j][1] = pack_f16x2(__bfloat162float(__ushort_as_bfloat16(__ldg(r4 + 2))),
+                                __bfloat162float(__ushort_as_bfloat16(__ldg(r4 + 3))));
+        } else {
+          qf[j][0] = pack_u16x2(__ldg(row + 16 * j + 2 * t), __ldg(row + 16 * j + 2 * t + 1));
+          qf[j][1] =
+              pack_u16x2(__ldg(row + 16 * j + 8 + 2 * t), __ldg(row + 16 * j + 8 + 2 * t + 1));
+        }
       }
     } else {
 #pragma unroll
@@ -970,11 +989,12 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       if (hd >= G) break;
       const int64_t row = q * G + hd;
       const float L = lrun[hi];
+      const float vs = kFp8 ? p.v_scale : 1.f;
       if (p.partial_mode) {
         for (int s = 0; s < partial_copies<kExchange>(p); ++s) {
           float* a = acc_dest(s) + row * D + lane * kPer;
 #pragma unroll
-          for (int i = 0; i < kPer; ++i) a[i] = o[hi][i];
+          for (int i = 0; i < kPer; ++i) a[i] = o[hi][i] * vs;
           if (lane == 0) {
             float* ml = ml_dest(s);
             ml[2 * row] = mrun[hi] * kLn2;
@@ -994,7 +1014,7 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       } else {
 #pragma unroll
         for (int i = 0; i < kPer; ++i)
-          p.out[row * D + lane * kPer + i] = __float2bfloat16_rn(L > 0.f ? o[hi][i] / L : 0.f);
+          p.out[row * D + lane * kPer + i] = __float2bfloat16_rn(L > 0.f ? o[hi][i] / L * vs : 0.f);
       }
     }
     if constexpr (kAppend) append_store<D>(p, q, clamped_len(p, q / Hkv), tid, kCT);
@@ -1061,12 +1081,15 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       fl_l[warp * kMaxGroup + 2 * t + 1] = lr1;
     }
     float* wa = fl_acc + warp * kMaxGroup * D;
+    // accumulator row -> dim: g and 8 + g (BF16), 2g and 2g + 1 (FP8 V order)
+    constexpr int kRowB = kFp8 ? 1 : 8;
+    const int da = kFp8 ? 2 * g : g;
 #pragma unroll
     for (int j = 0; j < kSlabs; ++j) {
-      wa[(2 * t) * D + 16 * j + g] = acc[j][0];
-      wa[(2 * t + 1) * D + 16 * j + g] = acc[j][1];
-      wa[(2 * t) * D + 16 * j + 8 + g] = acc[j][2];
-      wa[(2 * t + 1) * D + 16 * j + 8 + g] = acc[j][3];
+      wa[(2 * t) * D + 16 * j + da] = acc[j][0];
+      wa[(2 * t + 1) * D + 16 * j + da] = acc[j][1];
+      wa[(2 * t) * D + 16 * j + da + kRowB] = acc[j][2];
+      wa[(2 * t + 1) * D + 16 * j + da + kRowB] = acc[j][3];
     }
     if (thief && tid == 0) {
       const uint32_t d = atomicAdd(p.ws_counters, 1u);
@@ -1116,10 +1139,10 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
         p.out[row * D + d] = __float2bfloat16_rn(
             (O * a + wn * __bfloat162float(p.v_new[pair * D + d])) / (L * a + wn));
       } else if (complete && !p.partial_mode) {
-        p.out[row * D + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+        p.out[row * D + d] = __float2bfloat16_rn(L > 0.f ? O / L * (kFp8 ? p.v_scale : 1.f) : 0.f);
       } else if (complete) {
         for (int s = 0; s < partial_copies<kExchange>(p); ++s) {
-          acc_dest(s)[row * D + d] = O;
+          acc_dest(s)[row * D + d] = O * (kFp8 ? p.v_scale : 1.f);
           if (d == 0) {
             float* ml = ml_dest(s);
             ml[2 * row] = M * kLn2;
@@ -1243,15 +1266,31 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
         const int tok0 = (warp * kMB + mb) * 16;
         const int row = tok0 + (lane & 7) + ((lane >> 3) & 1) * 8;
         float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+        if constexpr (kFp8) {
+          // one 16-byte chunk of an FP8 row is a 16-dim slab: an x4 load
+          // covers slabs 2*s2 and 2*s2 + 1 of 16 tokens; each register holds
+          // 4 dims of one token, turned into two f16 pairs (values * 2^-8;
+          // the host folds 2^8 into the K and V scales)
 #pragma unroll
-        for (int j = 0; j < kSlabs; ++j) {
-          const int chunk = (j & 3) * 2 + (lane >> 4);
-          uint32_t a[4];
-          ldsm_x4(kbase + (j >> 2) * C::kBoxBytes + swz128(row, chunk), a);
-          if (j & 1)
-            mma_bf16_16816(c1, a, qf[j][0], qf[j][1]);
-          else
-            mma_bf16_16816(c0, a, qf[j][0], qf[j][1]);
+          for (int s2 = 0; s2 < kSlabs / 2; ++s2) {
+            uint32_t r[4];
+            ldsm_x4(kbase + swz128(row, 2 * s2 + (lane >> 4)), r);
+            const uint32_t a0[4] = {e4m3_01(r[0]), e4m3_01(r[1]), e4m3_23(r[0]), e4m3_23(r[1])};
+            const uint32_t a1[4] = {e4m3_01(r[2]), e4m3_01(r[3]), e4m3_23(r[2]), e4m3_23(r[3])};
+            mma_f16_16816(c0, a0, qf[2 * s2][0], qf[2 * s2][1]);
+            mma_f16_16816(c1, a1, qf[2 * s2 + 1][0], qf[2 * s2 + 1][1]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < kSlabs; ++j) {
+            const int chunk = (j & 3) * 2 + (lane >> 4);
+            uint32_t a[4];
+            ldsm_x4(kbase + (j >> 2) * C::kBoxBytes + swz128(row, chunk), a);
+            if (j & 1)
+              mma_bf16_16816(c1, a, qf[j][0], qf[j][1]);
+            else
+              mma_bf16_16816(c0, a, qf[j][0], qf[j][1]);
+          }
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -1285,8 +1324,13 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
         const float p2 = fast_exp2(sc[mb][2] - mu0), p3 = fast_exp2(sc[mb][3] - mu1);
         ps0 += p0 + p2;
         ps1 += p1 + p3;
-        pb[mb][0] = movmatrix_trans(pack_bf16x2(p0, p1));
-        pb[mb][1] = movmatrix_trans(pack_bf16x2(p2, p3));
+        if constexpr (kFp8) {
+          pb[mb][0] = movmatrix_trans(pack_f16x2(p0, p1));
+          pb[mb][1] = movmatrix_trans(pack_f16x2(p2, p3));
+        } else {
+          pb[mb][0] = movmatrix_trans(pack_bf16x2(p0, p1));
+          pb[mb][1] = movmatrix_trans(pack_bf16x2(p2, p3));
+        }
       }
       l_run[0] = l_run[0] * al0 + ps0;
       l_run[1] = l_run[1] * al1 + ps1;
@@ -1308,16 +1352,39 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
           keep01 = (ta < valid ? 0x0000ffffu : 0u) | (ta + 1 < valid ? 0xffff0000u : 0u);
           keep23 = (tb < valid ? 0x0000ffffu : 0u) | (tb + 1 < valid ? 0xffff0000u : 0u);
         }
+        if constexpr (kFp8) {
+          // transposed 16-bit loads of the FP8 V tile: a register holds
+          // dims (2g, 2g+1) of tokens (2t, 2t+1); regrouped by token pair per
+          // dim, MMA row g of slab j is dim 16j + 2g and row g + 8 is
+          // 16j + 2g + 1 (the flush writes the accumulator back that way)
+          const int rowk = tok0 + (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
-        for (int j = 0; j < kSlabs; ++j) {
-          const int chunk = (j & 3) * 2 + ((lane >> 3) & 1);
-          uint32_t a[4];
-          ldsm_x4_trans(vbase + (j >> 2) * C::kBoxBytes + swz128(row, chunk), a);
-          a[0] &= keep01;
-          a[1] &= keep01;
-          a[2] &= keep23;
-          a[3] &= keep23;
-          mma_bf16_16816(acc[j], a, pb[mb][0], pb[mb][1]);
+          for (int s2 = 0; s2 < kSlabs / 2; ++s2) {
+            uint32_t r[4];
+            ldsm_x4_trans(vbase + swz128(rowk, 2 * s2 + (lane >> 4)), r);
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              uint32_t a[4] = {e4m3_02(r[2 * h2]), e4m3_13(r[2 * h2]), e4m3_02(r[2 * h2 + 1]),
+                               e4m3_13(r[2 * h2 + 1])};
+              a[0] &= keep01;
+              a[1] &= keep01;
+              a[2] &= keep23;
+              a[3] &= keep23;
+              mma_f16_16816(acc[2 * s2 + h2], a, pb[mb][0], pb[mb][1]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < kSlabs; ++j) {
+            const int chunk = (j & 3) * 2 + ((lane >> 3) & 1);
+            uint32_t a[4];
+            ldsm_x4_trans(vbase + (j >> 2) * C::kBoxBytes + swz128(row, chunk), a);
+            a[0] &= keep01;
+            a[1] &= keep01;
+            a[2] &= keep23;
+            a[3] &= keep23;
+            mma_bf16_16816(acc[j], a, pb[mb][0], pb[mb][1]);
+          }
         }
       }
     }

@@ -7,6 +7,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 namespace adb {
@@ -161,6 +162,38 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                              uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  const __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Two e4m3 values to an f16x2 register holding them times 2^-8, exactly,
+// with integer operations only.  f16's exponent bias (15) exceeds e4m3's (7)
+// by 8 and both formats become subnormal at exponent field 0, so moving an
+// e4m3 byte's sign to bit 15 and its exponent and mantissa (bits 6..0) to
+// bits 13..7 gives the f16 of value * 2^-8 for every finite code (the NaN
+// code S.1111.111 becomes a finite number).  `w` holds the two bytes at
+// byte positions 1 and 3 (the low and high halves' top bytes).
+__device__ __forceinline__ uint32_t e4m3_pair_to_f16x2_scaled(uint32_t w) {
+  return (w & 0x80008000u) | ((w >> 1) & 0x3F803F80u);
+}
+
+// Pairs of the four e4m3 bytes (b0, b1, b2, b3) of x, as f16x2 times 2^-8:
+// (b0, b1), (b2, b3) -- consecutive elements -- and (b0, b2), (b1, b3).
+__device__ __forceinline__ uint32_t e4m3_01(uint32_t x) { return e4m3_pair_to_f16x2_scaled(__byte_perm(x, 0u, 0x1404u)); }
+__device__ __forceinline__ uint32_t e4m3_23(uint32_t x) { return e4m3_pair_to_f16x2_scaled(__byte_perm(x, 0u, 0x3424u)); }
+__device__ __forceinline__ uint32_t e4m3_02(uint32_t x) { return e4m3_pair_to_f16x2_scaled(__byte_perm(x, 0u, 0x2404u)); }
+__device__ __forceinline__ uint32_t e4m3_13(uint32_t x) { return e4m3_pair_to_f16x2_scaled(__byte_perm(x, 0u, 0x3414u)); }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

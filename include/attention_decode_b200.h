@@ -104,6 +104,21 @@ ADB_API int adb_decode(const void* q, const void* k, const void* v, const int32_
                        int64_t kv_len, int64_t head_dim, void* workspace,
                        size_t workspace_bytes, unsigned flags, int device, void* stream);
 
+/* Decode over an FP8 (e4m3, OCP "fn" encoding) K/V cache (no reference
+ * counterpart: the reference reads BF16 only).  k, v: [batch, kv_heads,
+ * kv_len, 128] e4m3 bytes, contiguous, 16-byte aligned; the values they
+ * stand for are k * k_scale and v * v_scale (per-tensor scales, positive and
+ * finite).  The result is the BF16 decode of those values (FP32 softmax and
+ * accumulation, Q rounded to FP16 for the tensor-core products), so it
+ * streams half the bytes of the BF16 path.  head_dim 128 only.  Other
+ * arguments as adb_decode (seqlens optional); workspace from
+ * adb_decode_workspace_size. */
+ADB_API int adb_decode_fp8(const void* q, const void* k, const void* v, const int32_t* seqlens,
+                           void* out, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                           int64_t kv_len, int64_t head_dim, float k_scale, float v_scale,
+                           void* workspace, size_t workspace_bytes, unsigned flags, int device,
+                           void* stream);
+
 /* One decode step of a serving loop with the new token appended (no
  * reference counterpart: the reference decodes a cache that already holds
  * every token).  Sequence b has seqlens[b] tokens cached in k_cache /

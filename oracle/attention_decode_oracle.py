@@ -64,6 +64,21 @@ def as_f32(x: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(x, dtype=np.float32)
 
 
+def e4m3_to_f32(bits: np.ndarray) -> np.ndarray:
+    """Decode FP8 e4m3 bytes (OCP "fn" encoding: 1 sign, 4 exponent bits with
+    bias 7, 3 mantissa bits, subnormals, no infinities, S.1111.111 is NaN) to
+    float32, exactly.  Used to check the FP8 K/V extension (not in the
+    reference, which reads BF16 only)."""
+    b = np.ascontiguousarray(bits, dtype=np.uint8).astype(np.int32)
+    sign = np.where(b & 0x80, -1.0, 1.0).astype(np.float32)
+    exp = (b >> 3) & 0xF
+    man = (b & 0x7).astype(np.float32)
+    normal = (1.0 + man / 8.0) * np.exp2(exp.astype(np.float32) - 7.0)
+    subnormal = (man / 8.0) * np.float32(2.0 ** -6)
+    out = sign * np.where(exp == 0, subnormal, normal).astype(np.float32)
+    return np.where((b & 0x7F) == 0x7F, np.float32(np.nan), out).astype(np.float32)
+
+
 # ---------------------------------------------------------------- reference
 def validate_shapes(q: np.ndarray, k: np.ndarray, v: np.ndarray) -> tuple[int, int, int, int, int, int]:
     """Shape contract of reference.py:15-34 (dtype/device/layout do not apply)."""

@@ -39,6 +39,19 @@ def oracle_reference(q, k, v, seqlens=None) -> torch.Tensor:
     return from_bits(oracle.f32_to_bf16_bits(out), q.device)
 
 
+def oracle_reference_fp8(q, k8, v8, k_scale, v_scale, seqlens=None) -> torch.Tensor:
+    """The CPU oracle over the values an e4m3 cache stands for (bytes decoded
+    by the oracle, times the per-tensor scales); BF16 on q's device."""
+    qb = to_bits(q)
+    kf = oracle.e4m3_to_f32(k8.detach().contiguous().cpu().view(torch.uint8).numpy()) * np.float32(k_scale)
+    vf = oracle.e4m3_to_f32(v8.detach().contiguous().cpu().view(torch.uint8).numpy()) * np.float32(v_scale)
+    if seqlens is None:
+        out = oracle.reference_fp32(qb, kf, vf)
+    else:
+        out = oracle.reference_varlen_fp32(qb, kf, vf, seqlens.cpu().numpy())
+    return from_bits(oracle.f32_to_bf16_bits(out), q.device)
+
+
 def inputs(device, length, dim=128, hkv=8, batch=1, seed=SEED, hq=32):
     """Seeded inputs generated on `device` (tests/test_extreme_decode.py:22-25)."""
     generator = torch.Generator(device=device).manual_seed(seed)

@@ -134,3 +134,15 @@ def test_varlen_zero_length_gives_zeros():
     out = oracle.reference_varlen_fp32(q, k, v, [0, 5, 300, 301])
     assert not np.any(out[0])
     np.testing.assert_allclose(out[3], oracle.reference_fp32(q[3:4], k[3:4], v[3:4])[0], rtol=1e-6, atol=1e-6)
+
+
+def test_e4m3_decoding_matches_torch():
+    """Pins the oracle's FP8 e4m3 decoder to torch's conversion on all 256 codes."""
+    import torch
+
+    codes = np.arange(256, dtype=np.uint8)
+    want = torch.from_numpy(codes).view(torch.float8_e4m3fn).float().numpy()
+    got = oracle.e4m3_to_f32(codes)
+    nan = np.isnan(want)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(got[~nan], want[~nan])
