@@ -57,6 +57,9 @@ def parse_args():
                    help="b200: this library; reference: the reference's FP32 algorithm on host cores; "
                         "ref-kernel: the reference's CUDA kernel rebuilt for sm_100a (baseline/build_ref_kernel.py); "
                         "sdpa: torch scaled_dot_product_attention (comparison arms, 1 GPU)")
+    p.add_argument("--kv", default="bf16", choices=("bf16", "fp8"),
+                   help="K/V cache element type: bf16 (the reference's) or fp8 e4m3 with per-tensor scales "
+                        "(attention_decode_fp8; head_dim 128)")
     p.add_argument("--transport", default="p2p", choices=("p2p", "nccl"),
                    help="cfg4 at N>1: state exchange through NVLink peer memory (p2p) or an NCCL all_gather")
     p.add_argument("--seed", type=int, default=2026)
@@ -293,6 +296,8 @@ def run_gpu_arm(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
     cfg = BASELINE_CONFIGS[args.config]
     sequence_sharded = cfg.name == "cfg4" and world > 1
+    if args.kv == "fp8" and (sequence_sharded or cfg.head_dim != 128):
+        raise SystemExit("bench: --kv fp8 runs single-GPU / batch-sharded configs with head_dim 128")
     q, k, v, seqlens = cfg.make_inputs(device, seed=args.seed + (0 if sequence_sharded else 1009 * rank))
     if sequence_sharded:
         from attention_decode import sharded
@@ -312,15 +317,35 @@ def run_gpu_arm(args):
         )
     else:
         bytes_per_rank = cfg.algorithmic_bytes(seqlens)
+        fp8_scales = None
+        if args.kv == "fp8":
+            # per-tensor e4m3 quantisation of the same K/V (amax -> 448); the
+            # step then reads one byte per element
+            ks = float(k.float().abs().max()) / 448.0
+            vs = float(v.float().abs().max()) / 448.0
+            k = (k.float() / ks).to(torch.float8_e4m3fn)
+            v = (v.float() / vs).to(torch.float8_e4m3fn)
+            torch.cuda.empty_cache()
+            fp8_scales = (ks, vs)
+            bytes_per_rank = (bytes_per_rank - 4 * cfg.batch * cfg.query_heads * cfg.head_dim) // 2 + \
+                4 * cfg.batch * cfg.query_heads * cfg.head_dim
         sets, kv_total = rotation_sets(cfg, device, args.seed + 1009 * rank, (q, k, v))
+        if fp8_scales is not None:
+            sets = [sets[0]] + [(qi, (ki.float() / fp8_scales[0]).to(torch.float8_e4m3fn),
+                                 (vi.float() / fp8_scales[1]).to(torch.float8_e4m3fn)) for qi, ki, vi in sets[1:]]
         n_sets = len(sets)
         rotation = [0]
+
+        def decode(qq, kk, vv, lens):
+            if fp8_scales is not None:
+                return ad.attention_decode_fp8(qq, kk, vv, lens, k_scale=fp8_scales[0], v_scale=fp8_scales[1])
+            return ad.attention_decode(qq, kk, vv, lens)
 
         def step():
             i = rotation[0]
             rotation[0] = (i + 1) % n_sets
             qq, kk, vv = sets[i]
-            return ad.attention_decode(qq, kk, vv, seqlens)
+            return decode(qq, kk, vv, seqlens)
 
         scaling = "weak"
         parallelism = f"batch-shard dp{world} (no collective)" if world > 1 else "single GPU"
@@ -337,7 +362,12 @@ def run_gpu_arm(args):
         full_k, full_v = (k, v) if not sequence_sharded else (None, None)
         if full_k is not None:
             nb = min(2, q.shape[0])
-            bits = [x[:nb].contiguous().cpu().view(torch.int16).numpy().view(np.uint16) for x in (q, full_k, full_v)]
+            if args.kv == "fp8":
+                bits = [q[:nb].contiguous().cpu().view(torch.int16).numpy().view(np.uint16)] + [
+                    oracle.e4m3_to_f32(x[:nb].contiguous().cpu().view(torch.uint8).numpy()) * np.float32(sc)
+                    for x, sc in ((full_k, fp8_scales[0]), (full_v, fp8_scales[1]))]
+            else:
+                bits = [x[:nb].contiguous().cpu().view(torch.int16).numpy().view(np.uint16) for x in (q, full_k, full_v)]
             if seqlens is None:
                 want = oracle.reference_fp32(*bits)
             else:
@@ -446,7 +476,7 @@ def run_gpu_arm(args):
         e2e_call = step_fn.with_query(q_dev)
     else:
         def e2e_call():
-            return ad.attention_decode(q_dev, k, v, lens_dev)
+            return decode(q_dev, k, v, lens_dev)
 
     def e2e_step():
         q_dev.copy_(q_host, non_blocking=True)
@@ -471,7 +501,7 @@ def run_gpu_arm(args):
 
     # ---- CPU baseline (rank 0, N=1)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.kv == "bf16":
         gbs, desc, _ = cpu_oracle_throughput(q, k, v, seqlens, cfg, budget_s=10.0)
         cpu = {"value": gbs, "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port", "sample": desc}
 
@@ -493,9 +523,9 @@ def run_gpu_arm(args):
             "higher_is_better": True,
             "scaling": scaling,
             "vs_baseline": None,
-            "dtype": "bf16",
+            "dtype": "bf16" if args.kv == "bf16" else "e4m3 K/V (per-tensor scales), bf16 Q/O, f16 products, f32 softmax",
             "data": "synthetic (seeded N(0,1) bf16 Q/K/V" + (", K ~ N(0,8^2) with x50 spikes" if cfg.extreme else "") + ")",
-            "config": dict(cfg.as_dict(), parallelism=parallelism, l2=l2_note),
+            "config": dict(cfg.as_dict(), parallelism=parallelism, l2=l2_note, kv=args.kv),
             "pct_of_8tbs": 100.0 * (total_bytes / (ms_step * 1e-3) / 1e9) / (NOMINAL_HBM_GBS * (world if not sequence_sharded else world)),
             "roofline": {
                 "bound": "hbm",
