@@ -550,19 +550,19 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
               for (int d = 0; d < D; ++d) p.out[row * D + d] = p.v_new[pair * D + d];
             append_store<D>(p, pair, 0, 0, 1);
           }
-          continue;
-        }
-        for (int64_t row = b * Hq; row < (b + 1) * Hq; ++row) {
-          if (!p.partial_mode) {
-            for (int d = 0; d < D; ++d) p.out[row * D + d] = __float2bfloat16_rn(0.f);
-            continue;
-          }
-          for (int s = 0; s < partial_copies<kExchange>(p); ++s) {
-            float* a = acc_dest(s);
-            float* ml = ml_dest(s);
-            for (int d = 0; d < D; ++d) a[row * D + d] = 0.f;
-            ml[2 * row] = neg_inf();
-            ml[2 * row + 1] = 0.f;
+        } else {
+          for (int64_t row = b * Hq; row < (b + 1) * Hq; ++row) {
+            if (!p.partial_mode) {
+              for (int d = 0; d < D; ++d) p.out[row * D + d] = __float2bfloat16_rn(0.f);
+              continue;
+            }
+            for (int s = 0; s < partial_copies<kExchange>(p); ++s) {
+              float* a = acc_dest(s);
+              float* ml = ml_dest(s);
+              for (int d = 0; d < D; ++d) a[row * D + d] = 0.f;
+              ml[2 * row] = neg_inf();
+              ml[2 * row + 1] = 0.f;
+            }
           }
         }
       }
@@ -613,75 +613,73 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       const uint64_t policy = l2_policy_evict_first();
       int64_t k = 0;  // stage sequence number (lane 0)
       bool ok = true;
-      // Paged cache: tokens per sub-box and sub-boxes per tile.
-      constexpr int kMaxSub = TT / 8;
+      // The whole producer warp runs the same control flow (the tile walks
+      // are deterministic, so every lane holds the same cursors); side
+      // effects belong to one lane -- lane 0 claims, writes the stage record
+      // and arrives on the barriers -- except a paged tile's sub-boxes, which
+      // lane j looks up and loads (one page each), so that small pages do not
+      // serialise on one thread.
       const int sub_shift = p.paged != 0 && p.page_shift < kTTShift ? p.page_shift : kTTShift;
-      const int n_sub = TT >> sub_shift;
-      // Lane 0: fill stage k with `m` (and its tile, if it is one).
+      const int n_sub = TT >> sub_shift;  // <= TT / 8 <= 32
+      // Fill stage k with `m` (and its tile, if it is one); called by all lanes.
       auto issue = [&](const TileMeta& m) -> bool {
         const int s = static_cast<int>(k % kStages);
         const bool is_tile = m.kind == kMetaOwn || m.kind == kMetaStolen;
-        // Paged: look the tile's pages up before waiting for the stage, so the
-        // block-table reads overlap the wait.  Sub-boxes past the sequence's
+        // Paged: lane j looks its page up before waiting for the stage, so the
+        // block-table read overlaps the wait.  Sub-boxes past the sequence's
         // last page reuse that page (their rows are masked as past the end).
-        int32_t blk[kMaxSub];
-        if (p.paged != 0 && is_tile) {
+        int32_t blk = 0;
+        if (p.paged != 0 && is_tile && lane < n_sub) {
           const int64_t tok0 = static_cast<int64_t>(m.tile_in_pair) * TT;
           const int64_t last_page = m.len > 0 ? (static_cast<int64_t>(m.len) - 1) >> p.page_shift : 0;
-          const int32_t* row = p.block_table + static_cast<int64_t>(m.b) * p.bt_stride;
-#pragma unroll
-          for (int j = 0; j < kMaxSub; ++j) {
-            if (j < n_sub) {
-              int64_t pg = (tok0 + (static_cast<int64_t>(j) << sub_shift)) >> p.page_shift;
-              if (pg > last_page) pg = last_page;
-              blk[j] = __ldg(row + pg);
-            }
-          }
+          int64_t pg = (tok0 + (static_cast<int64_t>(lane) << sub_shift)) >> p.page_shift;
+          if (pg > last_page) pg = last_page;
+          blk = __ldg(p.block_table + static_cast<int64_t>(m.b) * p.bt_stride + pg);
         }
-        if (k >= kStages &&
-            !mbar_wait(empty_bar(s), static_cast<uint32_t>((k / kStages) - 1) & 1u, abort_flag))
-          return false;
-        meta[s] = m;
+        bool waited = true;
+        if (k >= kStages)
+          waited = mbar_wait(empty_bar(s), static_cast<uint32_t>((k / kStages) - 1) & 1u, abort_flag);
+        if (!__all_sync(0xffffffffu, waited)) return false;
+        if (lane == 0) meta[s] = m;
         if (is_tile) {
-          mbar_arrive_expect_tx(full_bar(s), C::kStageBytes);
+          if (lane == 0) mbar_arrive_expect_tx(full_bar(s), C::kStageBytes);
+          __syncwarp();
           uint8_t* st = ring + static_cast<size_t>(s) * C::kStageBytes;
           if (p.paged == 0) {
-            const int y = m.tile_in_pair * TT;
-            const int z = static_cast<int>(m.b * Hkv + m.h);
+            if (lane == 0) {
+              const int y = m.tile_in_pair * TT;
+              const int z = static_cast<int>(m.b * Hkv + m.h);
 #pragma unroll
-            for (int h = 0; h < C::kHalves; ++h)
-              tma_load_3d(smem_u32(st + h * C::kBoxBytes), &tm_k, h * C::kBoxCols, y, z, full_bar(s), policy);
+              for (int h = 0; h < C::kHalves; ++h)
+                tma_load_3d(smem_u32(st + h * C::kBoxBytes), &tm_k, h * C::kBoxCols, y, z, full_bar(s), policy);
 #pragma unroll
-            for (int h = 0; h < C::kHalves; ++h)
-              tma_load_3d(smem_u32(st + (C::kHalves + h) * C::kBoxBytes), &tm_v, h * C::kBoxCols, y, z,
-                          full_bar(s), policy);
-          } else {
-            // Sub-box j lands at row j * rows of the stage's boxes; rows is a
-            // multiple of 8, so every sub-box starts on a 1024-byte swizzle
-            // atom and the layout equals one whole-tile load.
+              for (int h = 0; h < C::kHalves; ++h)
+                tma_load_3d(smem_u32(st + (C::kHalves + h) * C::kBoxBytes), &tm_v, h * C::kBoxCols, y, z,
+                            full_bar(s), policy);
+            }
+          } else if (lane < n_sub) {
+            // Sub-box `lane` lands at row lane * rows of the stage's boxes;
+            // rows is a multiple of 8, so every sub-box starts on a 1024-byte
+            // swizzle atom and the layout equals one whole-tile load.
             const int64_t tok0 = static_cast<int64_t>(m.tile_in_pair) * TT;
             const int page_mask = (1 << p.page_shift) - 1;
+            const int y = static_cast<int>((tok0 + (static_cast<int64_t>(lane) << sub_shift)) & page_mask);
+            const uint32_t off = static_cast<uint32_t>(lane << sub_shift) * 128u;
 #pragma unroll
-            for (int j = 0; j < kMaxSub; ++j) {
-              if (j >= n_sub) break;
-              const int y = static_cast<int>((tok0 + (static_cast<int64_t>(j) << sub_shift)) & page_mask);
-              const uint32_t off = static_cast<uint32_t>(j << sub_shift) * 128u;
-#pragma unroll
-              for (int h = 0; h < C::kHalves; ++h) {
-                const uint32_t dk = smem_u32(st + h * C::kBoxBytes) + off;
-                const uint32_t dv = smem_u32(st + (C::kHalves + h) * C::kBoxBytes) + off;
-                if (p.paged == 1) {
-                  const int z = blk[j] * static_cast<int>(Hkv) + m.h;
-                  tma_load_3d(dk, &tm_k, h * C::kBoxCols, y, z, full_bar(s), policy);
-                  tma_load_3d(dv, &tm_v, h * C::kBoxCols, y, z, full_bar(s), policy);
-                } else {
-                  tma_load_4d(dk, &tm_k, h * C::kBoxCols, m.h, y, blk[j], full_bar(s), policy);
-                  tma_load_4d(dv, &tm_v, h * C::kBoxCols, m.h, y, blk[j], full_bar(s), policy);
-                }
+            for (int h = 0; h < C::kHalves; ++h) {
+              const uint32_t dk = smem_u32(st + h * C::kBoxBytes) + off;
+              const uint32_t dv = smem_u32(st + (C::kHalves + h) * C::kBoxBytes) + off;
+              if (p.paged == 1) {
+                const int z = blk * static_cast<int>(Hkv) + m.h;
+                tma_load_3d(dk, &tm_k, h * C::kBoxCols, y, z, full_bar(s), policy);
+                tma_load_3d(dv, &tm_v, h * C::kBoxCols, y, z, full_bar(s), policy);
+              } else {
+                tma_load_4d(dk, &tm_k, h * C::kBoxCols, m.h, y, blk, full_bar(s), policy);
+                tma_load_4d(dv, &tm_v, h * C::kBoxCols, m.h, y, blk, full_bar(s), policy);
               }
             }
           }
-        } else {
+        } else if (lane == 0) {
           mbar_arrive(full_bar(s));
         }
         ++k;
@@ -691,7 +689,7 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       // Own phase: the static positions in order, then the claimable ones one
       // claim at a time (the next claim is in flight while the current tile
       // is issued).  One walk cursor per contiguous part of the order.
-      if (lane == 0) {
+      {
         if (t0 < t1) {
           const int64_t n = t1 - t0;
           const int64_t rot = rot_of(n, last_w);
@@ -716,10 +714,15 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
           auto valid = [&](unsigned long long w) {
             return static_cast<int64_t>(w & 0xffffffffull) + static_cast<int64_t>(w >> 32) < n_dyn;
           };
-          unsigned long long claim = n_dyn > 0 ? atomicAdd(p.ws_claims + c, 1ull) : 0ull;
+          auto claim_next = [&]() -> unsigned long long {
+            unsigned long long w = 0ull;
+            if (lane == 0) w = atomicAdd(p.ws_claims + c, 1ull);
+            return __shfl_sync(0xffffffffu, w, 0);
+          };
+          unsigned long long claim = n_dyn > 0 ? claim_next() : 0ull;
           for (int64_t pos = 0; pos < n_stat && ok; ++pos) ok = issue_pos(pos);
           while (ok && n_dyn > 0 && valid(claim)) {
-            const unsigned long long next = atomicAdd(p.ws_claims + c, 1ull);
+            const unsigned long long next = claim_next();
             ok = issue_pos(n_stat + static_cast<int64_t>(claim & 0xffffffffull));
             claim = next;
           }
@@ -784,7 +787,7 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
           back = __shfl_sync(0xffffffffu, back, 0);
           if (got == 0) continue;
           ++steals;
-          if (lane == 0) {
+          {
             Walk lw;
             locate(e_v - 1, lw);
             const int64_t rot_v = rot_of(n_v, lw);
@@ -795,11 +798,10 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
               ok = issue(meta_of(w, tt, kMetaStolen));
             }
           }
-          ok = __shfl_sync(0xffffffffu, ok, 0);
           if (!ok) break;
         }
       }
-      if (lane == 0 && ok) issue(meta_marker(kMetaEndAll));
+      if (ok) issue(meta_marker(kMetaEndAll));
       return;
     }
   }
