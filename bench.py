@@ -434,7 +434,7 @@ def run_gpu_arm(args):
     kernel_bytes = bytes_per_rank
     peak, peak_src = measured_peaks()
     achieved = kernel_bytes / (kernel_ms * 1e-3) / 1e9
-    traffic = profile_traffic(f"{cfg.name}_decode_stream_kernel")
+    traffic = profile_traffic(f"{cfg.name}_decode_stream_kernel" + ("_fp8" if args.kv == "fp8" else ""))
 
     # ---- optional: the same steps replayed from a CUDA graph
     graph_line = None
