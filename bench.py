@@ -53,10 +53,11 @@ def parse_args():
     p.add_argument("--steps", type=int, default=2000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--config", default="cfg2", choices=("cfg1", "cfg2", "cfg3", "cfg4", "cfg5"))
-    p.add_argument("--impl", default="b200", choices=("b200", "reference", "ref-kernel", "sdpa"),
+    p.add_argument("--impl", default="b200", choices=("b200", "reference", "ref-kernel", "sdpa", "fa2"),
                    help="b200: this library; reference: the reference's FP32 algorithm on host cores; "
                         "ref-kernel: the reference's CUDA kernel rebuilt for sm_100a (baseline/build_ref_kernel.py); "
-                        "sdpa: torch scaled_dot_product_attention (comparison arms, 1 GPU)")
+                        "sdpa: torch scaled_dot_product_attention; fa2: flash_attn_with_kvcache "
+                        "(comparison arms, 1 GPU)")
     p.add_argument("--kv", default="bf16", choices=("bf16", "fp8"),
                    help="K/V cache element type: bf16 (the reference's) or fp8 e4m3 with per-tensor scales "
                         "(attention_decode_fp8; head_dim 128)")
@@ -436,6 +437,21 @@ def run_gpu_arm(args):
     achieved = kernel_bytes / (kernel_ms * 1e-3) / 1e9
     traffic = profile_traffic(f"{cfg.name}_decode_stream_kernel" + ("_fp8" if args.kv == "fp8" else ""))
 
+    # ---- per-step distribution: events around each step of a separate pass
+    # (the events between steps cut the programmatic-launch overlap, so the
+    # median here sits above us_per_step)
+    pct_n = min(args.steps, 300)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(pct_n)]
+    torch.cuda.synchronize(device)
+    for a, b in ev:
+        a.record(stream)
+        step()
+        b.record(stream)
+    torch.cuda.synchronize(device)
+    per_step = sorted(a.elapsed_time(b) * 1e3 for a, b in ev)
+    pct = {"p10": per_step[len(per_step) // 10], "p50": per_step[len(per_step) // 2],
+           "p90": per_step[(9 * len(per_step)) // 10], "steps": pct_n}
+
     # ---- optional: the same steps replayed from a CUDA graph
     graph_line = None
     if args.graph > 0 and not sequence_sharded:
@@ -551,6 +567,7 @@ def run_gpu_arm(args):
             },
             "gpu_launches": launches_timed,
             "graph": graph_line,
+            "per_step_us": pct,
             "clocks": clocks,
             "correctness": check,
         }
@@ -626,6 +643,20 @@ def run_comparison_arm(args):
             return mod.forward(qq, kk, vv)
 
         label = "reference csrc/decode.cu rebuilt for sm_100a (capability gate relaxed, otherwise unchanged)"
+    elif args.impl == "fa2":
+        try:
+            from flash_attn import flash_attn_with_kvcache
+        except Exception as exc:  # not installed or no kernels for this build
+            return unavailable(f"flash_attn import failed: {type(exc).__name__}: {exc}"[:300])
+        cache_lens = seqlens.to(torch.int32) if seqlens is not None else None
+
+        def call(qq, kk, vv):
+            # flash_attn reads [B, S, H, D] caches and [B, 1, Hq, D] queries;
+            # the layout change of the cache is made once per input set, below
+            out = flash_attn_with_kvcache(qq.transpose(1, 2), kk, vv, cache_seqlens=cache_lens)
+            return out.transpose(1, 2)
+
+        label = "flash_attn.flash_attn_with_kvcache (cache transposed to [B, S, Hkv, D] once, outside the timing)"
     else:
         import torch.nn.functional as F
 
@@ -637,11 +668,18 @@ def run_comparison_arm(args):
             return F.scaled_dot_product_attention(qq, kk, vv, attn_mask=mask, enable_gqa=True)
 
         label = "torch.nn.functional.scaled_dot_product_attention(enable_gqa=True" + (", boolean padding mask)" if mask is not None else ")")
-    out = call(q, k, v)
     want = ad.attention_decode(q, k, v, seqlens)
-    torch.cuda.synchronize(device)
-    max_err = float((out.float() - want.float()).abs().max())
     sets, _ = rotation_sets(cfg, device, args.seed + 1009 * rank, (q, k, v))
+    if args.impl == "fa2":
+        sets = [(qi, ki.transpose(1, 2).contiguous(), vi.transpose(1, 2).contiguous()) for qi, ki, vi in sets]
+        q, k, v = sets[0]
+        torch.cuda.empty_cache()
+    try:
+        out = call(q, k, v)
+        torch.cuda.synchronize(device)
+    except Exception as exc:
+        return unavailable(f"{args.impl} call failed: {type(exc).__name__}: {exc}"[:300])
+    max_err = float((out.float() - want.float()).abs().max())
     rotation = [0]
 
     def step():
@@ -700,7 +738,7 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)
-    if args.impl in ("ref-kernel", "sdpa"):
+    if args.impl in ("ref-kernel", "sdpa", "fa2"):
         return run_comparison_arm(args)
     return run_gpu_arm(args)
 

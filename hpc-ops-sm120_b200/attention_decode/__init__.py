@@ -452,11 +452,24 @@ def read_error_flag(device=0, reset=True) -> int:
 class _Extension:
     """Object with the reference extension's ``forward(q, k, v)`` method
     (csrc/binding.cpp:6-8), so code that calls ``_get_extension().forward``
-    keeps working."""
+    keeps working, plus the compatible additions: optional ``seqlens`` on
+    ``forward``, ``forward_partial`` (unnormalised state for sequence
+    sharding) and ``combine`` (merge of R partial states)."""
 
     @staticmethod
-    def forward(q, k, v):
-        return attention_decode(q, k, v)
+    def forward(q, k, v, seqlens=None):
+        return attention_decode(q, k, v, seqlens)
+
+    @staticmethod
+    def forward_partial(q, k, v, seqlens=None):
+        return attention_decode_partial(q, k, v, seqlens)
+
+    @staticmethod
+    def combine(acc, ml):
+        """acc FP32 [R, B, Hq, D], ml FP32 [R, B, Hq, 2] -> BF16 [B, Hq, 1, D]."""
+        parts, batch, q_heads, head_dim = acc.shape
+        out = combine_partials(acc.reshape(parts, batch * q_heads, head_dim), ml.reshape(parts, batch * q_heads, 2))
+        return out.view(batch, q_heads, 1, head_dim)
 
 
 @lru_cache(maxsize=1)

@@ -269,3 +269,7 @@ def attention_decode_sequence_sharded(q, k_local, v_local, group=None, seqlens_l
         return step().clone()
     finally:
         step.release()
+
+
+# The name the sequence-sharded entry point is planned under.
+attention_decode_sharded = attention_decode_sequence_sharded

@@ -134,3 +134,16 @@ def test_append_arguments_are_checked_on_host():
     lib = _lib.load_library()
     rc = lib.adb_decode_append(None, None, None, None, None, None, None, 1, 32, 8, 128, 128, None, 0, 0, 0, None)
     assert rc == _lib.ADB_ERR_INVALID_ARGUMENT and "append" in _lib.last_error(lib)
+
+
+def test_extension_object_has_the_reference_method_and_the_additions():
+    """attention_decode/__init__.py:8-23 binds `forward`; the additions keep it."""
+    import inspect
+
+    import attention_decode
+    from attention_decode import sharded
+
+    ext = attention_decode._get_extension()
+    assert list(inspect.signature(ext.forward).parameters)[:3] == ["q", "k", "v"]
+    assert callable(ext.forward_partial) and callable(ext.combine)
+    assert sharded.attention_decode_sharded is sharded.attention_decode_sequence_sharded

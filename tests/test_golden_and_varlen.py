@@ -125,3 +125,15 @@ def test_combine_skips_empty_parts(device):
 def test_no_device_error_flag_after_tests(device):
     torch.cuda.synchronize(device)
     assert ad.read_error_flag(device.index or 0, reset=True) == 0
+
+
+def test_extension_partial_and_combine_match_forward(device, record_property):
+    """forward_partial on two token halves + combine == forward on all tokens."""
+    q, k, v = inputs(device, 3001, 128, 8, batch=2, hq=32, seed=808)
+    ext = ad._get_extension()
+    full = ext.forward(q, k, v)
+    halves = [ext.forward_partial(q, k[:, :, a:b].contiguous(), v[:, :, a:b].contiguous()) for a, b in ((0, 1500), (1500, 3001))]
+    acc = torch.stack([h[0] for h in halves])
+    ml = torch.stack([h[1] for h in halves])
+    merged = ext.combine(acc, ml)
+    check(merged, full, q, record_property, atol=1e-2, rtol=2.0**-7)
