@@ -61,6 +61,9 @@ def parse_args():
     p.add_argument("--kv", default="bf16", choices=("bf16", "fp8"),
                    help="K/V cache element type: bf16 (the reference's) or fp8 e4m3 with per-tensor scales "
                         "(attention_decode_fp8; head_dim 128)")
+    p.add_argument("--scaling", default="weak", choices=("weak", "strong"),
+                   help="N>1 batch-sharded configs: every rank runs the whole config (weak) or its share "
+                        "of one global batch (strong: B/N sequences, token-balanced for cfg3)")
     p.add_argument("--transport", default="p2p", choices=("p2p", "nccl"),
                    help="cfg4 at N>1: state exchange through NVLink peer memory (p2p) or an NCCL all_gather")
     p.add_argument("--seed", type=int, default=2026)
@@ -299,7 +302,19 @@ def run_gpu_arm(args):
     sequence_sharded = cfg.name == "cfg4" and world > 1
     if args.kv == "fp8" and (sequence_sharded or cfg.head_dim != 128):
         raise SystemExit("bench: --kv fp8 runs single-GPU / batch-sharded configs with head_dim 128")
-    q, k, v, seqlens = cfg.make_inputs(device, seed=args.seed + (0 if sequence_sharded else 1009 * rank))
+    strong = args.scaling == "strong" and world > 1 and not sequence_sharded
+    shard_index = None
+    if strong:
+        from attention_decode import sharded
+
+        lengths = cfg.make_seqlens(args.seed)
+        if lengths is not None:  # balance the streamed tokens across ranks
+            shard_index = sharded.balance_by_tokens(lengths.tolist(), world)[rank]
+        else:
+            shard_index = list(range(cfg.batch))[sharded.batch_shard(cfg.batch, rank, world)]
+        q, k, v, seqlens = cfg.make_inputs(device, seed=args.seed, batch_slice=shard_index)
+    else:
+        q, k, v, seqlens = cfg.make_inputs(device, seed=args.seed + (0 if sequence_sharded else 1009 * rank))
     if sequence_sharded:
         from attention_decode import sharded
 
@@ -317,7 +332,11 @@ def run_gpu_arm(args):
             else f"sequence-shard sp{world} (all_gather of partial states over NCCL)"
         )
     else:
-        bytes_per_rank = cfg.algorithmic_bytes(seqlens)
+        if strong:
+            tokens = int(seqlens.clamp(0, cfg.kv_len).sum()) if seqlens is not None else len(shard_index) * cfg.kv_len
+            bytes_per_rank = 2 * 2 * cfg.head_dim * cfg.kv_heads * tokens + 4 * len(shard_index) * cfg.query_heads * cfg.head_dim
+        else:
+            bytes_per_rank = cfg.algorithmic_bytes(seqlens)
         fp8_scales = None
         if args.kv == "fp8":
             # per-tensor e4m3 quantisation of the same K/V (amax -> 448); the
@@ -348,8 +367,12 @@ def run_gpu_arm(args):
             qq, kk, vv = sets[i]
             return decode(qq, kk, vv, seqlens)
 
-        scaling = "weak"
-        parallelism = f"batch-shard dp{world} (no collective)" if world > 1 else "single GPU"
+        scaling = "strong" if strong else "weak"
+        if strong:
+            parallelism = (f"batch-shard dp{world}, one global batch split over ranks "
+                           f"({'token-balanced' if seqlens is not None else 'B/N sequences'} per rank, no collective)")
+        else:
+            parallelism = f"batch-shard dp{world} (no collective)" if world > 1 else "single GPU"
 
     # Correctness gate on a subset of sequences (full rows, CPU oracle).
     out = step()
@@ -411,6 +434,8 @@ def run_gpu_arm(args):
     total_bytes = bytes_per_rank * (world if not sequence_sharded else 1)
     if sequence_sharded:
         total_bytes = cfg.algorithmic_bytes()
+    if strong:
+        total_bytes = cfg.algorithmic_bytes(cfg.make_seqlens(args.seed))
     value = total_bytes / (ms_step * 1e-3) / 1e9
 
     # ---- dominant kernel: event pairs around each streaming-kernel launch

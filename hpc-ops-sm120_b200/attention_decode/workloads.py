@@ -122,19 +122,25 @@ class BaselineConfig:
         lens[positions] = torch.tensor([1, 7, self.kv_len])
         return lens.to(torch.int32)
 
-    def make_inputs(self, device, seed: int = 2026, batch_slice: slice | None = None):
+    def make_inputs(self, device, seed: int = 2026, batch_slice=None):
         """(q, k, v, seqlens) on `device`.  K/V are generated directly on the
-        device (seeded); ``batch_slice`` selects a contiguous subset of the
-        sequences (batch sharding) with identical values to the full batch."""
+        device (seeded); ``batch_slice`` (a slice or a list of sequence
+        indices) selects a subset of the sequences (batch sharding) with
+        identical values to the full batch."""
         device = torch.device(device)
         seqlens = self.make_seqlens(seed)
-        rows = range(self.batch)[batch_slice] if batch_slice is not None else range(self.batch)
+        if batch_slice is None:
+            rows = list(range(self.batch))
+        elif isinstance(batch_slice, slice):
+            rows = list(range(self.batch)[batch_slice])
+        else:
+            rows = [int(b) for b in batch_slice]
         q_full = torch.randn(
             (self.batch, self.query_heads, 1, self.head_dim),
             generator=torch.Generator(device="cpu").manual_seed(seed),
             dtype=torch.float32,
         ).to(torch.bfloat16)
-        q = q_full[rows.start : rows.stop].contiguous().to(device)
+        q = q_full[rows].contiguous().to(device)
         kv_shape = (len(rows), self.kv_heads, self.kv_len, self.head_dim)
         k = torch.empty(kv_shape, dtype=torch.bfloat16, device=device)
         v = torch.empty(kv_shape, dtype=torch.bfloat16, device=device)
@@ -149,7 +155,7 @@ class BaselineConfig:
                 heads = torch.arange(self.kv_heads, device=device)
                 k[i, heads, spike] *= 50
         if seqlens is not None:
-            seqlens = seqlens[rows.start : rows.stop].contiguous().to(device)
+            seqlens = seqlens[rows].contiguous().to(device)
         return q, k, v, seqlens
 
 

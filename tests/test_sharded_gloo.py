@@ -136,3 +136,17 @@ def test_batch_shard_slices_cover_the_batch():
 
 if __name__ == "__main__":
     sys.exit(pytest.main([__file__, "-q"]))
+
+
+def test_batch_shards_of_baseline_inputs_reproduce_the_full_batch():
+    """A rank's share of one global batch (slice or token-balanced index list)
+    holds exactly the full batch's rows, so strong scaling shards one problem."""
+    from attention_decode.workloads import BaselineConfig
+
+    cfg = BaselineConfig("small", 6, 8, 2, 64, 40, varlen=True, extreme=True)
+    q, k, v, lens = cfg.make_inputs("cpu", seed=11)
+    parts = sharded.balance_by_tokens(lens.tolist(), 3)
+    for part in parts + [list(range(6))[sharded.batch_shard(6, 1, 3)]]:
+        qs, ks, vs, ls = cfg.make_inputs("cpu", seed=11, batch_slice=part)
+        assert torch.equal(qs, q[part]) and torch.equal(ks, k[part]) and torch.equal(vs, v[part])
+        assert torch.equal(ls, lens[part])
