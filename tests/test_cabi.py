@@ -147,3 +147,27 @@ def test_extension_object_has_the_reference_method_and_the_additions():
     assert list(inspect.signature(ext.forward).parameters)[:3] == ["q", "k", "v"]
     assert callable(ext.forward_partial) and callable(ext.combine)
     assert sharded.attention_decode_sharded is sharded.attention_decode_sequence_sharded
+
+
+def test_header_and_library_serve_a_plain_c_host(tmp_path):
+    """A C program compiled against include/*.h and linked to the library
+    (what a cgo / JNI / C++ host does) gets the documented answers."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    lib = _lib.load_library()
+    lib_dir = str(_lib.LIB_PATH.parent)
+    exe = tmp_path / "c_abi_host"
+    build = subprocess.run(
+        [cc, "-std=c99", "-Wall", "-Werror", f"-I{ROOT / 'include'}", str(ROOT / "tests" / "c_abi_host.c"),
+         f"-L{lib_dir}", "-l:" + _lib.LIB_NAME, f"-Wl,-rpath,{lib_dir}", "-o", str(exe)],
+        capture_output=True, text=True,
+    )
+    assert build.returncode == 0, build.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, run.stdout + run.stderr
+    assert "all host checks passed" in run.stdout
+    del lib
