@@ -17,9 +17,10 @@ kernel stores its partial states into every rank's exchange buffer over
 NVLink and a merge kernel combines them on each rank, or with
 `--transport nccl` the states are all-gathered over NCCL: strong scaling).
 
-`--impl reference` times the reference's FP32 algorithm on the host cores
-(the numpy oracle restating attention_decode/reference.py:47-60) on a bounded
-sample of the same workload, on rank 0 only.
+`--impl reference` times the reference's CPU path on the host cores: the
+torch FP32 decode of attention_decode/reference.py:47-60 (restated with the
+same torch calls in oracle/reference_torch.py, all host threads) on the whole
+workload (cfg5: its first 16 sequences), on rank 0 only.
 """
 
 from __future__ import annotations
@@ -172,80 +173,90 @@ class ClockSampler:
         }
 
 
-# ---------------------------------------------------------------- CPU oracle
-def cpu_oracle_throughput(q, k, v, seqlens, cfg, budget_s: float):
-    """Time the numpy restatement of the reference FP32 path on host cores on
-    whole sequences of this workload until `budget_s` is spent.  Returns
-    (GB/s of algorithmic bytes, sample description, seconds measured)."""
-    from oracle import attention_decode_oracle as oracle
+# ---------------------------------------------------------------- CPU baseline
+CPU_SAMPLE_BYTES = 1_100_000_000  # a step of the CPU arm streams at most ~1.1 GB
 
-    def bits(t):
-        return t.contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
 
-    batch = q.shape[0]
-    lens = seqlens.cpu().numpy() if seqlens is not None else None
-    done_bytes, elapsed, seqs = 0, 0.0, 0
-    b = 0
-    # Move one sequence at a time to the host (the transfer is not timed).
-    while elapsed < budget_s and seqs < 64 * batch:
-        qb, kb, vb = bits(q[b : b + 1]), bits(k[b : b + 1]), bits(v[b : b + 1])
-        n = int(lens[b]) if lens is not None else cfg.kv_len
+def cpu_sample_sequences(cfg, seqlens=None) -> int:
+    """Sequences of the workload one CPU step covers: the whole batch when its
+    bytes fit CPU_SAMPLE_BYTES (cfg1-cfg4), else the leading sequences that do
+    (cfg5: 16 of 128)."""
+    per_seq = [cfg.algorithmic_bytes(None) // cfg.batch] * cfg.batch if seqlens is None else [
+        2 * 2 * cfg.head_dim * cfg.kv_heads * int(n) + 4 * cfg.query_heads * cfg.head_dim
+        for n in seqlens.clamp(0, cfg.kv_len).tolist()]
+    total, n = 0, 0
+    for b in per_seq:
+        if n and total + b > CPU_SAMPLE_BYTES:
+            break
+        total += b
+        n += 1
+    return n
+
+
+def cpu_reference_step(q, k, v, seqlens):
+    """One decode step of the reference's CPU path (reference.py:47-60,
+    restated with the same torch calls in oracle/reference_torch.py)."""
+    from oracle import reference_torch
+
+    if seqlens is None:
+        return reference_torch.reference_fp32(q, k, v)
+    return reference_torch.reference_varlen_fp32(q, k, v, seqlens.tolist())
+
+
+def cpu_step_bytes(cfg, q, seqlens) -> int:
+    tokens = q.shape[0] * cfg.kv_len if seqlens is None else int(seqlens.clamp(0, cfg.kv_len).sum())
+    return 2 * 2 * cfg.head_dim * cfg.kv_heads * tokens + 4 * q.shape[0] * cfg.query_heads * cfg.head_dim
+
+
+def cpu_baseline_throughput(q, k, v, seqlens, cfg, budget_s: float):
+    """The reference's CPU path on the host cores (all threads) over the
+    same inputs as the GPU arm, copied to the host (untimed); whole steps are
+    repeated until `budget_s` is spent.  Returns (GB/s, cores, sample)."""
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    n = cpu_sample_sequences(cfg, seqlens.cpu() if seqlens is not None else None)
+    qc, kc, vc = (x[:n].cpu() for x in (q, k, v))
+    lc = seqlens[:n].cpu() if seqlens is not None else None
+    step_bytes = cpu_step_bytes(cfg, qc, lc)
+    cpu_reference_step(qc, kc, vc, lc)  # warm-up
+    elapsed, steps = 0.0, 0
+    while elapsed < budget_s and steps < 200:
         t0 = time.perf_counter()
-        if lens is None:
-            oracle.reference_fp32(qb, kb, vb)
-        else:
-            oracle.reference_varlen_fp32(qb, kb, vb, lens[b : b + 1])
+        cpu_reference_step(qc, kc, vc, lc)
         elapsed += time.perf_counter() - t0
-        done_bytes += 2 * 2 * cfg.head_dim * cfg.kv_heads * n + 2 * 2 * cfg.query_heads * cfg.head_dim
-        seqs += 1
-        b = (b + 1) % batch
-    sample = f"{seqs} whole sequences of {cfg.name} (one at a time, numpy FP32, {elapsed:.1f} s)"
-    return done_bytes / elapsed / 1e9, sample, elapsed
+        steps += 1
+    what = "the whole step" if n == cfg.batch else f"{n} of {cfg.batch} sequences per step"
+    sample = (f"{what} of {cfg.name} ({step_bytes / 1e9:.3f} GB), {steps} steps in {elapsed:.1f} s; "
+              f"torch FP32 on CPU with {cores} threads (the reference's reference_fp32 calls, "
+              f"oracle/reference_torch.py)")
+    return step_bytes * steps / elapsed / 1e9, cores, sample
 
 
 def run_reference_arm(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
-    sys.path.insert(0, os.path.join(ROOT, "hpc-ops-sm120_b200"))
     from attention_decode.workloads import BASELINE_CONFIGS
-    from oracle import attention_decode_oracle as oracle
 
     cfg = BASELINE_CONFIGS[args.config]
     cores = os.cpu_count() or 1
-    # Per-step sample: one (batch, kv_head) pair of the workload, FP32 on the
-    # host with every BLAS thread; calibrated so the whole run stays short.
-    gen = np.random.default_rng(args.seed)
-    length = cfg.kv_len if not cfg.varlen else cfg.kv_len // 2
-    group = cfg.group
-
-    def sample(pairs):
-        q = oracle.f32_to_bf16_bits(gen.standard_normal((1, group * pairs, 1, cfg.head_dim), dtype=np.float32))
-        k = oracle.f32_to_bf16_bits(gen.standard_normal((1, pairs, length, cfg.head_dim), dtype=np.float32))
-        v = oracle.f32_to_bf16_bits(gen.standard_normal((1, pairs, length, cfg.head_dim), dtype=np.float32))
-        return q, k, v
-
-    probe = sample(1)
-    t0 = time.perf_counter()
-    oracle.reference_fp32(*probe)
-    t_pair = max(time.perf_counter() - t0, 1e-5)
-    budget = 90.0
-    pairs = int(max(1, min(cfg.batch * cfg.kv_heads, budget / max(args.steps + args.warmup, 1) / t_pair)))
-    pairs = min(pairs, 64)
-    inputs = sample(pairs)
-    step_bytes = 2 * 2 * cfg.head_dim * pairs * length + 2 * 2 * group * pairs * cfg.head_dim
+    torch.set_num_threads(cores)
+    # The same seeded workload as the GPU arm, generated on the host; a step
+    # is the whole workload (or, for cfg5, its leading 16 sequences).
+    seqlens = cfg.make_seqlens(args.seed)
+    n = cpu_sample_sequences(cfg, seqlens)
+    q, k, v, lens = cfg.make_inputs("cpu", seed=args.seed, batch_slice=slice(0, n))
+    step_bytes = cpu_step_bytes(cfg, q, lens)
     for _ in range(args.warmup):
-        oracle.reference_fp32(*inputs)
-    times = []
+        cpu_reference_step(q, k, v, lens)
     t_all = time.perf_counter()
     for _ in range(args.steps):
-        t0 = time.perf_counter()
-        oracle.reference_fp32(*inputs)
-        times.append(time.perf_counter() - t0)
-    total = time.perf_counter() - t_all
-    sec_per_step = total / args.steps
+        cpu_reference_step(q, k, v, lens)
+    sec_per_step = (time.perf_counter() - t_all) / args.steps
     value = step_bytes / sec_per_step / 1e9
-    desc = f"{pairs} (batch, kv_head) pair(s) x {length} tokens of {cfg.name} per step (numpy FP32 oracle, BLAS threads={cores})"
+    what = "the whole step" if n == cfg.batch else f"{n} of {cfg.batch} sequences per step"
+    desc = (f"{what} of {cfg.name} ({step_bytes / 1e9:.3f} GB); torch FP32 on CPU with {cores} threads "
+            f"(the reference's reference_fp32 calls, oracle/reference_torch.py)")
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -259,7 +270,7 @@ def run_reference_arm(args):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic (seeded N(0,1), rounded to bf16)",
+        "data": "synthetic (seeded N(0,1) bf16 Q/K/V" + (", K ~ N(0,8^2) with x50 spikes" if cfg.extreme else "") + ")",
         "config": cfg.as_dict(),
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -405,15 +416,30 @@ def run_gpu_arm(args):
 
     lib = _lib.load_library()
     launches0 = ctypes_count(lib)
+    stream = torch.cuda.current_stream(device)
+    # Clock samples cover the warm-up and the timed region; the sampler starts
+    # first so that the GPU never idles between the warm-up and the timing (an
+    # idle B200 lowers its SM clock within a fraction of a second and the first
+    # steps after that run slower).
+    sampler = ClockSampler(device)
+    sampler.start()
+    time.sleep(0.3)
+    # Warm-up: the W steps asked for, then enough further steps to run the GPU
+    # for ~30 ms (SM clocks back at their loaded operating point), right
+    # before the timed steps.
+    w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0.record(stream)
     for _ in range(args.warmup):
+        step()
+    w1.record(stream)
+    torch.cuda.synchronize(device)
+    est_s = max(w0.elapsed_time(w1) * 1e-3 / args.warmup, 1e-6)
+    settle_steps = int(min(5000, max(0, 0.03 / est_s - args.warmup)))
+    for _ in range(settle_steps):
         step()
     torch.cuda.synchronize(device)
 
     # ---- device-timed region
-    sampler = ClockSampler(device)
-    sampler.start()
-    time.sleep(0.3)
-    stream = torch.cuda.current_stream(device)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize(device)
@@ -543,8 +569,8 @@ def run_gpu_arm(args):
     # ---- CPU baseline (rank 0, N=1)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.kv == "bf16":
-        gbs, desc, _ = cpu_oracle_throughput(q, k, v, seqlens, cfg, budget_s=10.0)
-        cpu = {"value": gbs, "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port", "sample": desc}
+        gbs, cores, desc = cpu_baseline_throughput(q, k, v, seqlens, cfg, budget_s=10.0)
+        cpu = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port", "sample": desc}
 
     if sequence_sharded or n_sets == 1:
         l2_note = "KV cache larger than the 126 MB L2: every step streams from HBM, no flush needed"
@@ -559,6 +585,7 @@ def run_gpu_arm(args):
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
+            "warmup_settle_steps": settle_steps,
             "ms_per_step": ms_step,
             "us_per_step": ms_step * 1e3,
             "higher_is_better": True,

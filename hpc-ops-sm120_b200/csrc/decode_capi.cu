@@ -99,6 +99,7 @@ const Variant kVariants[] = {
     make_fp8_variant<4, 2, 6>("d128_fp8_tt128_s6"),
     make_fp8_variant<4, 1, 8>("d128_fp8_tt64_s8"),
     make_fp8_variant<8, 1, 5>("d128_fp8_w8_tt128_s5"),
+    make_variant<128, 8, 1, 3, true>("d128_tma_w8_tt128_s3"),
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 constexpr int kDefaultTma128 = 0, kSmallTma128 = 1, kDefaultTma64 = 3, kSmallTma64 = 4;
@@ -513,9 +514,10 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
   // the extra segments it creates (about 192 tiles per CTA).
   static const int forced_steals = env_int("ADB_MAX_STEALS", -1);
   static const int claim_divisor = env_int("ADB_CLAIM_DIVISOR", 4);
+  static const int steal_min_tiles = env_int("ADB_STEAL_MIN_TILES", 192);
   const int64_t tiles_per_cta =
       s.P * ((s.S + var.tile_tokens - 1) / var.tile_tokens) / plan.num_ctas;
-  p.max_steals = forced_steals >= 0 ? forced_steals : (tiles_per_cta >= 192 ? adb::kMaxSteals : 0);
+  p.max_steals = forced_steals >= 0 ? forced_steals : (tiles_per_cta >= steal_min_tiles ? adb::kMaxSteals : 0);
   p.claim_divisor = claim_divisor >= 2 ? claim_divisor : 2;
   p.steal = (allow_steal && var.tma && !deterministic_mode() && p.max_steals > 0) ? 1 : 0;
   p.dyn_capacity = plan.dyn_slots;
@@ -949,6 +951,30 @@ int adb_timing_enable(int enable) {
   t_timing.enabled = enable != 0;
   return ADB_OK;
 }
+
+#ifdef ADB_TRACE
+// Diagnostic build only: copies the per-CTA timeline of launch slot `slot`
+// (0 or 1) into `host` (adb::kTraceCtas * 16 u64) and returns the slot the
+// next launch will write.
+__attribute__((visibility("default"))) int adb_trace_read(unsigned long long* host, int slot) {
+  cudaError_t e = cudaMemcpyFromSymbol(host, adb::g_adb_trace, sizeof(unsigned long long) * adb::kTraceCtas * 16,
+                                       sizeof(unsigned long long) * adb::kTraceCtas * 16 * (slot & 1));
+  if (e != cudaSuccess) return cuda_fail(e, "reading the trace");
+  unsigned int next = 0;
+  e = cudaMemcpyFromSymbol(&next, adb::g_adb_trace_launch, sizeof(next));
+  if (e != cudaSuccess) return cuda_fail(e, "reading the trace");
+  return static_cast<int>(next & 1u);
+}
+
+// Diagnostic build only: the per-launch log (256 x 2 u64) and the number of
+// launches so far.
+__attribute__((visibility("default"))) int adb_launch_log_read(unsigned long long* host, unsigned* launches) {
+  cudaError_t e = cudaMemcpyFromSymbol(host, adb::g_adb_launch_log, sizeof(unsigned long long) * 512);
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(launches, adb::g_adb_trace_launch, sizeof(unsigned));
+  if (e != cudaSuccess) return cuda_fail(e, "reading the launch log");
+  return ADB_OK;
+}
+#endif
 
 int adb_timing_read(double* total_ms, int64_t* launches) {
   if (total_ms == nullptr || launches == nullptr)

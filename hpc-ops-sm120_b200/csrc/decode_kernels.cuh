@@ -66,6 +66,26 @@ constexpr int kStealChunk = 4;          // most tiles one steal takes
 constexpr int kStealMinRemaining = 4;   // a victim with fewer claimable tiles is left alone
 constexpr int kPrefetchTiles = 6;       // tiles warmed in L2 before the previous grid is done
 
+#ifdef ADB_TRACE
+// Diagnostic build only (-DADB_TRACE): per-CTA timeline of the last two
+// launches, read back with adb_trace_read.  Per CTA: [0] smid | cta << 32,
+// [1] entry, [2] after the grid dependency wait, [3] first tile arrived,
+// [4] own range done, [5] exit (globaltimer ns), [6] own tiles | other tiles
+// << 32, [7] merges | merge ns << 16, [8] producer's first load issued,
+// [9] producer done, [10] producer ns waiting for free stages, [11] consumer
+// (warp 0) ns waiting for full stages, [12] consumer ns from a full stage to
+// its release.
+constexpr int kTraceCtas = 1024;
+__device__ unsigned long long g_adb_trace[2][kTraceCtas][16];
+__device__ unsigned int g_adb_trace_launch = 0;
+// Per launch (ring of 256): [0] earliest return from the grid dependency wait,
+// [1] exit of the last CTA.
+__device__ unsigned long long g_adb_launch_log[256][2];
+#define ADB_TRACE_ONLY(...) __VA_ARGS__
+#else
+#define ADB_TRACE_ONLY(...)
+#endif
+
 // ---------------------------------------------------------------- exchange
 // Sequence sharding over NVLink peer memory.  Every rank owns one exchange
 // buffer in its own HBM, mapped into every other rank's process (CUDA IPC):
@@ -308,8 +328,12 @@ struct StreamCfg {
   static constexpr int kThreads = (kWarps + (kTma ? 1 : 0)) * 32;
   static constexpr int kConsumerThreads = kWarps * 32;
   static constexpr int kRingBytes = kRingStages * kStageBytes;
-  static constexpr int kFlushAccBytes = kWarps * kMaxGroup * D * 4;
-  static constexpr int kFlushMlBytes = kWarps * kMaxGroup * 2 * 4;
+  // Warps whose states meet in shared memory when a segment is flushed; with
+  // more consumer warps, warp w + kFlushWarps first folds its state into
+  // warp w's registers through the same buffer.
+  static constexpr int kFlushWarps = kWarps < 4 ? kWarps : 4;
+  static constexpr int kFlushAccBytes = kFlushWarps * kMaxGroup * D * 4;
+  static constexpr int kFlushMlBytes = kFlushWarps * kMaxGroup * 2 * 4;
   static constexpr int kBarBytes = 2 * kRingStages * 8;
   static constexpr int kMetaBytes = kRingStages * 32;
   static constexpr int kTableBytes = (kMaxTableBatches + 1) * 8;
@@ -392,10 +416,11 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   // 128-byte-swizzled TMA boxes need 1024-byte aligned shared addresses.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* ring = smem;
-  float* fl_acc = reinterpret_cast<float*>(smem + C::kRingBytes);  // [kWarps][8][D]
-  float* fl_m = fl_acc + kWarps * kMaxGroup * D;                    // [kWarps][8]
-  float* fl_l = fl_m + kWarps * kMaxGroup;                          // [kWarps][8]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(fl_l + kWarps * kMaxGroup);
+  constexpr int kFW = C::kFlushWarps;
+  float* fl_acc = reinterpret_cast<float*>(smem + C::kRingBytes);  // [kFW][8][D]
+  float* fl_m = fl_acc + kFW * kMaxGroup * D;                       // [kFW][8]
+  float* fl_l = fl_m + kFW * kMaxGroup;                             // [kFW][8]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(fl_l + kFW * kMaxGroup);
   TileMeta* meta = reinterpret_cast<TileMeta*>(bars + 2 * C::kRingStages);
   int64_t* table = reinterpret_cast<int64_t*>(meta + C::kRingStages);  // [B+1] varlen
   int64_t* misc = table + kMaxTableBatches + 1;
@@ -410,6 +435,7 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   // Let the next kernel in the stream launch early; it must wait for this
   // grid (griddepcontrol.wait) before touching memory, as this one does.
   griddep_launch_dependents();
+  ADB_TRACE_ONLY(const uint64_t tr_entry = global_timer_ns(); uint64_t tr_wait = 0, tr_first = 0, tr_own = 0, tr_merge_ns = 0; uint32_t tr_merges = 0, tr_own_tiles = 0, tr_other_tiles = 0; uint64_t tr_c1 = 0, tr_cwait = 0, tr_cbusy = 0;)
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t B = p.batch, Hkv = p.kv_heads, S = p.kv_len;
@@ -433,27 +459,49 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       prefetch_tensormap(&tm_v);
     }
   }
+  // ------------------------------------------------------------ uniform range
+  // With one length for every sequence the CTA's tile range follows from the
+  // parameters alone, so it is computed before the grid dependency wait and
+  // the first loads go out as soon as the previous grid is done.
+  const int64_t nt_uniform = (S + TT - 1) / TT;
+  int64_t nt_total = 0, t0 = 0, t1 = 0;
+  Walk first_w, last_w;  // tiles t0 and t1 - 1 (valid when t0 < t1)
+  first_w = Walk{0, 0, 0, 0, 0};
+  last_w = first_w;
+  bool have_table = false;
+  if (p.seqlens == nullptr) {
+    nt_total = P * nt_uniform;
+    t0 = c * nt_total / nc;
+    t1 = (c + 1) * nt_total / nc;
+    if (t0 < t1) {
+      const int64_t b0 = t0 / nt_uniform / Hkv, b1 = (t1 - 1) / nt_uniform / Hkv;
+      walk_locate(first_w, p, b0, b0 * Hkv * nt_uniform, t0, TT);
+      walk_locate(last_w, p, b1, b1 * Hkv * nt_uniform, t1 - 1, TT);
+    }
+  }
   // While the previous grid in the stream drains, warm L2 with the first
   // tiles this CTA will stream (uniform layout: the range follows from the
   // parameters alone).  A prefetch reads nothing into the CTA and L2 is the
   // coherence point, so later loads still see whatever the previous grid
-  // writes.  Long ranges (load balancing on) gain nothing from it.
+  // writes.  These first positions are never claimable by other CTAs unless
+  // the range is shorter than kPrefetchTiles, where a stolen tile only costs
+  // one wasted prefetch.
   if constexpr (kTma) {
-    if (warp == kWarps && lane == 0 && p.seqlens == nullptr && p.paged == 0 && !p.steal) {
-      const int64_t ntu = (S + TT - 1) / TT;
-      const int64_t ntt = P * ntu;
-      const int64_t a = c * ntt / nc, e = (c + 1) * ntt / nc, n = e - a;
+    if (warp == kWarps && lane == 0 && p.seqlens == nullptr && p.paged == 0) {
+      const int64_t ntu = nt_uniform;
+      const int64_t a = t0, e = t1, n = e - a;
       if (n > 0) {
         // processing order: the part of the last pair that continues into
         // the next CTA's range first, then the range in order
-        const int64_t last_tile = (e - 1) % ntu;
+        const int64_t last_tile = last_w.tile;
         int64_t rot = last_tile + 1 < ntu ? (last_tile + 1 < n ? last_tile + 1 : n) : 0;
         if (rot == n) rot = 0;
         const int64_t count = n < kPrefetchTiles ? n : kPrefetchTiles;
         for (int64_t i = 0; i < count; ++i) {
           const int64_t t = i < rot ? e - rot + i : a + i - rot;
-          const int y = static_cast<int>((t % ntu) * TT);
-          const int z = static_cast<int>(t / ntu);
+          const int64_t pr = t / ntu;
+          const int y = static_cast<int>((t - pr * ntu) * TT);
+          const int z = static_cast<int>(pr);
 #pragma unroll
           for (int h = 0; h < C::kHalves; ++h) {
             tma_prefetch_3d(&tm_k, h * C::kBoxCols, y, z);
@@ -466,6 +514,10 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   __syncthreads();
   // No global memory is touched before the previous grid in the stream is done.
   griddep_wait();
+#ifdef ADB_TRACE
+  tr_wait = global_timer_ns();
+  if (tid == 0) atomicMin(&g_adb_launch_log[g_adb_trace_launch & 255u][0], tr_wait);
+#endif
 
   // Partial-state stores go to the local arrays, or (peer exchange) to this
   // rank's slot in every rank's exchange buffer, at the parity of the call
@@ -482,20 +534,8 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   };
 
   // ------------------------------------------------------------ tile range
-  const int64_t nt_uniform = (S + TT - 1) / TT;
-  int64_t nt_total, t0, t1;
-  Walk first_w, last_w;  // tiles t0 and t1 - 1 (valid when t0 < t1)
-  bool have_table = false;
-  if (p.seqlens == nullptr) {
-    nt_total = P * nt_uniform;
-    t0 = c * nt_total / nc;
-    t1 = (c + 1) * nt_total / nc;
-    if (t0 < t1) {
-      const int64_t b0 = t0 / nt_uniform / Hkv, b1 = (t1 - 1) / nt_uniform / Hkv;
-      walk_locate(first_w, p, b0, b0 * Hkv * nt_uniform, t0, TT);
-      walk_locate(last_w, p, b1, b1 * Hkv * nt_uniform, t1 - 1, TT);
-    }
-  } else {
+  // (varlen: computed after the wait below, from the sequence lengths)
+  if (p.seqlens != nullptr) {
     // Pass 1: total tiles.  Pass 2: per-batch tile prefix (kept in shared
     // memory when the batch is small) and the batches holding tiles t0 and
     // t1 - 1.  CTA 0 also writes the rows of empty sequences.
@@ -611,6 +651,7 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       // K/V tiles are read exactly once: mark them first to leave L2, so the
       // segment states that other CTAs merge later stay resident.
       const uint64_t policy = l2_policy_evict_first();
+      ADB_TRACE_ONLY(uint64_t tr_pwait = 0, tr_pfirst = 0;)
       int64_t k = 0;  // stage sequence number (lane 0)
       bool ok = true;
       // The whole producer warp runs the same control flow (the tile walks
@@ -637,8 +678,10 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
           blk = __ldg(p.block_table + static_cast<int64_t>(m.b) * p.bt_stride + pg);
         }
         bool waited = true;
+        ADB_TRACE_ONLY(const uint64_t tr_p0 = global_timer_ns();)
         if (k >= kStages)
           waited = mbar_wait(empty_bar(s), static_cast<uint32_t>((k / kStages) - 1) & 1u, abort_flag);
+        ADB_TRACE_ONLY(tr_pwait += global_timer_ns() - tr_p0; if (k == 0) tr_pfirst = global_timer_ns();)
         if (!__all_sync(0xffffffffu, waited)) return false;
         if (lane == 0) meta[s] = m;
         if (is_tile) {
@@ -714,17 +757,25 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
           auto valid = [&](unsigned long long w) {
             return static_cast<int64_t>(w & 0xffffffffull) + static_cast<int64_t>(w >> 32) < n_dyn;
           };
-          auto claim_next = [&]() -> unsigned long long {
-            unsigned long long w = 0ull;
-            if (lane == 0) w = atomicAdd(p.ws_claims + c, 1ull);
-            return __shfl_sync(0xffffffffu, w, 0);
+          // Two claims are kept in flight: lane 0 issues the atomic one
+          // tile ahead and the warp reads its result a tile later, so the
+          // claim's round trip overlaps the wait for a free stage.  A claim
+          // is never wasted: once one is invalid every later one is too.
+          auto claim_issue = [&]() -> unsigned long long {
+            return lane == 0 ? atomicAdd(p.ws_claims + c, 1ull) : 0ull;
           };
-          unsigned long long claim = n_dyn > 0 ? claim_next() : 0ull;
+          unsigned long long c1 = 0ull, c2 = 0ull;
+          if (n_dyn > 0) {
+            c1 = claim_issue();
+            c2 = claim_issue();
+          }
           for (int64_t pos = 0; pos < n_stat && ok; ++pos) ok = issue_pos(pos);
-          while (ok && n_dyn > 0 && valid(claim)) {
-            const unsigned long long next = claim_next();
+          while (ok && n_dyn > 0) {
+            const unsigned long long claim = __shfl_sync(0xffffffffu, c1, 0);
+            if (!valid(claim)) break;
+            c1 = c2;
+            c2 = claim_issue();
             ok = issue_pos(n_stat + static_cast<int64_t>(claim & 0xffffffffull));
-            claim = next;
           }
         }
         if (ok) ok = issue(meta_marker(kMetaEndOwn));
@@ -802,6 +853,14 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
         }
       }
       if (ok) issue(meta_marker(kMetaEndAll));
+#ifdef ADB_TRACE
+      if (lane == 0 && c < kTraceCtas) {
+        unsigned long long* r = g_adb_trace[g_adb_trace_launch & 1u][c];
+        r[8] = tr_pfirst;
+        r[9] = global_timer_ns();
+        r[10] = tr_pwait;
+      }
+#endif
       return;
     }
   }
@@ -866,6 +925,7 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   // heads are loaded together and folded in.
   auto merge_pair = [&](int64_t q, int64_t first, int64_t last, int64_t n_thieves) {
     __threadfence();
+    ADB_TRACE_ONLY(const uint64_t tr_m0 = global_timer_ns();)
     constexpr int kPer = D / 32;
     float mrun[C::kHeadsPerWarp], lrun[C::kHeadsPerWarp], o[C::kHeadsPerWarp][kPer];
 #pragma unroll
@@ -1020,6 +1080,7 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       }
     }
     if constexpr (kAppend) append_store<D>(p, q, clamped_len(p, q / Hkv), tid, kCT);
+    ADB_TRACE_ONLY(tr_merge_ns += global_timer_ns() - tr_m0; ++tr_merges;)
   };
 
   // Commit `add` for pair q (after this CTA's segment of q is written) and
@@ -1076,23 +1137,54 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       lr0 += __shfl_xor_sync(0xffffffffu, lr0, o);
       lr1 += __shfl_xor_sync(0xffffffffu, lr1, o);
     }
-    if (g == 0) {
-      fl_m[warp * kMaxGroup + 2 * t] = m_run[0];
-      fl_m[warp * kMaxGroup + 2 * t + 1] = m_run[1];
-      fl_l[warp * kMaxGroup + 2 * t] = lr0;
-      fl_l[warp * kMaxGroup + 2 * t + 1] = lr1;
-    }
-    float* wa = fl_acc + warp * kMaxGroup * D;
     // accumulator row -> dim: g and 8 + g (BF16), 2g and 2g + 1 (FP8 V order)
     constexpr int kRowB = kFp8 ? 1 : 8;
     const int da = kFp8 ? 2 * g : g;
+    auto publish = [&](int slot_w) {
+      if (g == 0) {
+        fl_m[slot_w * kMaxGroup + 2 * t] = m_run[0];
+        fl_m[slot_w * kMaxGroup + 2 * t + 1] = m_run[1];
+        fl_l[slot_w * kMaxGroup + 2 * t] = lr0;
+        fl_l[slot_w * kMaxGroup + 2 * t + 1] = lr1;
+      }
+      float* wa = fl_acc + slot_w * kMaxGroup * D;
 #pragma unroll
-    for (int j = 0; j < kSlabs; ++j) {
-      wa[(2 * t) * D + 16 * j + da] = acc[j][0];
-      wa[(2 * t + 1) * D + 16 * j + da] = acc[j][1];
-      wa[(2 * t) * D + 16 * j + da + kRowB] = acc[j][2];
-      wa[(2 * t + 1) * D + 16 * j + da + kRowB] = acc[j][3];
+      for (int j = 0; j < kSlabs; ++j) {
+        wa[(2 * t) * D + 16 * j + da] = acc[j][0];
+        wa[(2 * t + 1) * D + 16 * j + da] = acc[j][1];
+        wa[(2 * t) * D + 16 * j + da + kRowB] = acc[j][2];
+        wa[(2 * t + 1) * D + 16 * j + da + kRowB] = acc[j][3];
+      }
+    };
+    if constexpr (kWarps > kFW) {
+      // Warp w + kFW hands its state to warp w (same lane layout, so each
+      // lane reads back exactly the values its counterpart wrote) ...
+      if (warp >= kFW) publish(warp - kFW);
+      bar();
+      if (warp < kFW) {
+        const float mo0 = fl_m[warp * kMaxGroup + 2 * t], mo1 = fl_m[warp * kMaxGroup + 2 * t + 1];
+        const float lo0 = fl_l[warp * kMaxGroup + 2 * t], lo1 = fl_l[warp * kMaxGroup + 2 * t + 1];
+        const float M0 = fmaxf(m_run[0], mo0), M1 = fmaxf(m_run[1], mo1);
+        const float u0 = M0 == neg_inf() ? 0.f : M0, u1 = M1 == neg_inf() ? 0.f : M1;
+        const float a0 = fast_exp2(m_run[0] - u0), b0 = fast_exp2(mo0 - u0);
+        const float a1 = fast_exp2(m_run[1] - u1), b1 = fast_exp2(mo1 - u1);
+        const float* wa = fl_acc + warp * kMaxGroup * D;
+#pragma unroll
+        for (int j = 0; j < kSlabs; ++j) {
+          acc[j][0] = acc[j][0] * a0 + wa[(2 * t) * D + 16 * j + da] * b0;
+          acc[j][1] = acc[j][1] * a1 + wa[(2 * t + 1) * D + 16 * j + da] * b1;
+          acc[j][2] = acc[j][2] * a0 + wa[(2 * t) * D + 16 * j + da + kRowB] * b0;
+          acc[j][3] = acc[j][3] * a1 + wa[(2 * t + 1) * D + 16 * j + da + kRowB] * b1;
+        }
+        lr0 = lr0 * a0 + lo0 * b0;
+        lr1 = lr1 * a1 + lo1 * b1;
+        m_run[0] = M0;
+        m_run[1] = M1;
+      }
+      bar();
     }
+    // ... and warps 0..kFW-1 meet in shared memory.
+    if (warp < kFW) publish(warp);
     if (thief && tid == 0) {
       const uint32_t d = atomicAdd(p.ws_counters, 1u);
       if (d < p.dyn_capacity) {
@@ -1124,11 +1216,11 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       const int hd = e / D, d = e - hd * D;
       float M = neg_inf();
 #pragma unroll
-      for (int ww = 0; ww < kWarps; ++ww) M = fmaxf(M, fl_m[ww * kMaxGroup + hd]);
+      for (int ww = 0; ww < kFW; ++ww) M = fmaxf(M, fl_m[ww * kMaxGroup + hd]);
       const float Mu = M == neg_inf() ? 0.f : M;
       float L = 0.f, O = 0.f;
 #pragma unroll
-      for (int ww = 0; ww < kWarps; ++ww) {
+      for (int ww = 0; ww < kFW; ++ww) {
         const float f = fast_exp2(fl_m[ww * kMaxGroup + hd] - Mu);
         L += f * fl_l[ww * kMaxGroup + hd];
         O += f * fl_acc[(ww * kMaxGroup + hd) * D + d];
@@ -1189,8 +1281,10 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
     const uint8_t* st = ring + static_cast<size_t>(s) * C::kStageBytes;
     TileMeta m;
     if constexpr (kTma) {
+      ADB_TRACE_ONLY(const uint64_t tr_c0 = global_timer_ns();)
       if (!mbar_wait(full_bar(s), static_cast<uint32_t>(k / kStages) & 1u, abort_flag)) break;
       m = meta[s];
+      ADB_TRACE_ONLY(tr_c1 = global_timer_ns(); tr_cwait += tr_c1 - tr_c0; if (k == 0) tr_first = tr_c1;)
     } else {
       // Generic path (K/V not 16-byte aligned): no producer and no stealing;
       // every warp copies its own rows with 2-byte loads into the same
@@ -1231,6 +1325,7 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
 
     if (m.kind == kMetaEndOwn) {
       release();
+      ADB_TRACE_ONLY(tr_own = global_timer_ns();)
       if (cur_pair >= 0) flush(cur_pair, false, cur_toff, cur_nt, cur_count);
       flush_empty(inc_next, inc_last);
       cur_pair = -1;
@@ -1392,6 +1487,7 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
     }
     release();
     ++cur_count;
+    ADB_TRACE_ONLY(if (thief_phase) ++tr_other_tiles; else ++tr_own_tiles; tr_cbusy += global_timer_ns() - tr_c1;)
   }
 
   // ------------------------------------------------------------ exit
@@ -1400,6 +1496,21 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   // each CTA's stores (peer ones included) are released at GPU scope before
   // it counts itself finished; the last CTA, having observed every count,
   // fences at system scope and raises the flags, which releases them all.
+#ifdef ADB_TRACE
+  if (tid == 0 && c < kTraceCtas) {
+    unsigned long long* r = g_adb_trace[g_adb_trace_launch & 1u][c];
+    r[0] = static_cast<unsigned long long>(smid()) | (static_cast<unsigned long long>(c) << 32);
+    r[1] = tr_entry;
+    r[2] = tr_wait;
+    r[3] = tr_first;
+    r[4] = tr_own;
+    r[5] = global_timer_ns();
+    r[6] = tr_own_tiles | (static_cast<unsigned long long>(tr_other_tiles) << 32);
+    r[7] = tr_merges | (tr_merge_ns << 16);
+    r[11] = tr_cwait;
+    r[12] = tr_cbusy;
+  }
+#endif
   __threadfence();
   bar();
   if (tid == 0) misc[46] = atomicAdd(p.ws_counters + 1, 1u) == static_cast<uint32_t>(nc - 1);
@@ -1416,6 +1527,11 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
     if (tid == 0) {
       p.ws_counters[0] = 0u;
       p.ws_counters[1] = 0u;
+#ifdef ADB_TRACE
+      g_adb_launch_log[g_adb_trace_launch & 255u][1] = global_timer_ns();
+      g_adb_launch_log[(g_adb_trace_launch + 1u) & 255u][0] = ~0ull;
+      g_adb_trace_launch += 1u;
+#endif
       if constexpr (kExchange) {
         __threadfence_system();
         const uint32_t call = x_epoch(p) + 1u;

@@ -146,3 +146,22 @@ def test_e4m3_decoding_matches_torch():
     nan = np.isnan(want)
     assert np.array_equal(np.isnan(got), nan)
     assert np.array_equal(got[~nan], want[~nan])
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c.name for c in CASES])
+def test_torch_restatement_matches_reference_golden(case):
+    """Pins oracle/reference_torch.py (the CPU baseline the benchmark times)
+    against the same golden outputs of the reference's reference.py."""
+    import torch
+
+    from oracle import reference_torch
+
+    q, k, v, lens = case.inputs()
+    tq, tk, tv = (torch.from_numpy(x.view(np.int16)).view(torch.bfloat16) for x in (q, k, v))
+    if lens is None:
+        out32 = reference_torch.reference_fp32(tq, tk, tv).numpy()
+    else:
+        out32 = reference_torch.reference_varlen_fp32(tq, tk, tv, lens).numpy()
+    want32 = GOLDEN[f"{case.name}/out_fp32"]
+    assert out32.shape == want32.shape
+    np.testing.assert_allclose(out32, want32, rtol=1e-5, atol=1e-5)

@@ -6,8 +6,8 @@ to a different allocator, or a serving loop that must not enter
 cudaMalloc/cudaFree because they synchronise the device.  adb_decode_no_alloc
 serves them with a fixed scratch array inside the library.  Here it must
 give the same results as the regular entry point (adb_decode, reached through
-attention_decode), within the tolerance of the other parity tests, on two
-calls in a row (the second call finds the previous call's leftovers in the
+attention_decode) and as the CPU oracle, within the tolerance of the other
+parity tests, on two calls in a row (the second call finds the previous call's leftovers in the
 shared array), and refuse a problem whose scratch does not fit.
 
 This file sorts last so a stopping run has run every other test before it; it
@@ -22,7 +22,7 @@ import pytest
 import torch
 
 from attention_decode import _lib, attention_decode
-from helpers import ATOL, RTOL, inputs
+from helpers import ATOL, RTOL, check, inputs, oracle_reference
 
 pytestmark = pytest.mark.gpu
 
@@ -54,12 +54,14 @@ def test_no_alloc_matches_regular_entry_point(batch, hq, hkv, length, dim, lens,
     q, k, v = inputs(cuda_device, length, dim, hkv, batch=batch, hq=hq, seed=4242)
     seqlens = torch.tensor(lens, dtype=torch.int32, device=cuda_device) if lens is not None else None
     expected = attention_decode(q, k, v, seqlens)
+    want = oracle_reference(q, k, v, seqlens)
     for _ in range(2):
         out = torch.full_like(q, float("nan"))
         _lib.check(lib, _no_alloc(lib, q, k, v, seqlens, out))
         torch.cuda.synchronize(cuda_device)
         assert torch.isfinite(out).all().item()
         torch.testing.assert_close(out, expected, atol=ATOL, rtol=RTOL)
+        check(out, want, q)
 
 
 def test_no_alloc_rejects_problems_larger_than_its_workspace(cuda_device):
