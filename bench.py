@@ -11,8 +11,9 @@ than the 126 MB L2, so consecutive steps stream from HBM without a flush.
 Metric: achieved HBM GB/s = algorithmic bytes per step (valid K+V, Q read,
 O write) / step time, summed over ranks; us/step is reported beside it.
 Multi-GPU (torchrun, one process per GPU, NCCL): cfg1/2/3/5 are batch-sharded
-with no collective (each rank runs its own full copy of the workload: weak
-scaling); cfg4 is sequence-sharded (each rank holds S/N tokens; the decode
+with no collective; by default one global batch is split over the ranks
+(strong scaling: B/N sequences per rank, token-balanced for cfg3), and
+`--scaling weak` gives every rank a whole replica instead; cfg4 is sequence-sharded (each rank holds S/N tokens; the decode
 kernel stores its partial states into every rank's exchange buffer over
 NVLink and a merge kernel combines them on each rank, or with
 `--transport nccl` the states are all-gathered over NCCL: strong scaling).
@@ -62,9 +63,10 @@ def parse_args():
     p.add_argument("--kv", default="bf16", choices=("bf16", "fp8"),
                    help="K/V cache element type: bf16 (the reference's) or fp8 e4m3 with per-tensor scales "
                         "(attention_decode_fp8; head_dim 128)")
-    p.add_argument("--scaling", default="weak", choices=("weak", "strong"),
-                   help="N>1 batch-sharded configs: every rank runs the whole config (weak) or its share "
-                        "of one global batch (strong: B/N sequences, token-balanced for cfg3)")
+    p.add_argument("--scaling", default="strong", choices=("weak", "strong"),
+                   help="N>1 batch-sharded configs: each rank decodes its share of one global batch "
+                        "(strong, the default: B/N sequences, token-balanced for cfg3) or a whole replica "
+                        "of the config (weak)")
     p.add_argument("--transport", default="p2p", choices=("p2p", "nccl"),
                    help="cfg4 at N>1: state exchange through NVLink peer memory (p2p) or an NCCL all_gather")
     p.add_argument("--seed", type=int, default=2026)
@@ -315,6 +317,14 @@ def run_gpu_arm(args):
         raise SystemExit("bench: --kv fp8 runs single-GPU / batch-sharded configs with head_dim 128")
     strong = args.scaling == "strong" and world > 1 and not sequence_sharded
     shard_index = None
+    if strong and cfg.batch < world:
+        # fewer sequences than ranks: there is no batch split to measure
+        if rank == 0:
+            print(json.dumps({"impl": "b200", "metric": METRIC, "config": cfg.as_dict(), "n_gpus": world,
+                              "unavailable": f"{cfg.name} has {cfg.batch} sequence(s): a batch split over "
+                                             f"{world} ranks leaves ranks empty (use --scaling weak)"}), flush=True)
+        dist.destroy_process_group()
+        return 0
     if strong:
         from attention_decode import sharded
 
@@ -433,7 +443,9 @@ def run_gpu_arm(args):
         step()
     w1.record(stream)
     torch.cuda.synchronize(device)
-    est_s = max(w0.elapsed_time(w1) * 1e-3 / args.warmup, 1e-6)
+    # every rank runs the same number of steps (sequence-sharded steps
+    # exchange states with all ranks), so the count comes from one value
+    est_s = max_over_ranks(max(w0.elapsed_time(w1) * 1e-3 / args.warmup, 1e-6), world, device)
     settle_steps = int(min(5000, max(0, 0.03 / est_s - args.warmup)))
     for _ in range(settle_steps):
         step()

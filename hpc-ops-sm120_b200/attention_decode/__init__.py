@@ -210,12 +210,19 @@ def attention_decode(q, k, v, seqlens=None):
     8.  ``seqlens`` (optional int32 [B] CUDA tensor) restricts sequence b to
     its first seqlens[b] tokens of the padded cache; a length of 0 gives a
     zero row.  Returns a new [B,Hq,1,D] BF16 tensor.  Uses the current CUDA
-    stream.
+    stream.  The type and device checks are the reference's Python ones
+    (attention_decode/__init__.py:35-38); the rest are done in C++ by the
+    extension's ``forward`` with the reference's messages.
     """
-    _validate(q, k, v, seqlens)
-    out = _torch().empty_like(q)
-    _launch(q, k, v, seqlens, out=out)
-    return out
+    torch = _torch()
+    Tensor = torch.Tensor
+    if not (isinstance(q, Tensor) and isinstance(k, Tensor) and isinstance(v, Tensor)):
+        raise TypeError("Q, K, and V must be tensors")
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise ValueError("Q, K, and V must be CUDA tensors")
+    if seqlens is not None and not isinstance(seqlens, Tensor):
+        raise TypeError("seqlens must be a tensor")
+    return _get_extension().forward(q, k, v, seqlens)
 
 
 def attention_decode_fp8(q, k, v, seqlens=None, *, k_scale=1.0, v_scale=1.0):
@@ -449,30 +456,20 @@ def read_error_flag(device=0, reset=True) -> int:
     return flag.value
 
 
-class _Extension:
-    """Object with the reference extension's ``forward(q, k, v)`` method
-    (csrc/binding.cpp:6-8), so code that calls ``_get_extension().forward``
-    keeps working, plus the compatible additions: optional ``seqlens`` on
-    ``forward``, ``forward_partial`` (unnormalised state for sequence
-    sharding) and ``combine`` (merge of R partial states)."""
-
-    @staticmethod
-    def forward(q, k, v, seqlens=None):
-        return attention_decode(q, k, v, seqlens)
-
-    @staticmethod
-    def forward_partial(q, k, v, seqlens=None):
-        return attention_decode_partial(q, k, v, seqlens)
-
-    @staticmethod
-    def combine(acc, ml):
-        """acc FP32 [R, B, Hq, D], ml FP32 [R, B, Hq, 2] -> BF16 [B, Hq, 1, D]."""
-        parts, batch, q_heads, head_dim = acc.shape
-        out = combine_partials(acc.reshape(parts, batch * q_heads, head_dim), ml.reshape(parts, batch * q_heads, 2))
-        return out.view(batch, q_heads, 1, head_dim)
-
-
 @lru_cache(maxsize=1)
 def _get_extension():
+    """The PyTorch C++ extension (adb_torch_ext.so, built in-tree from
+    csrc/torch_binding.cpp): ``forward(q, k, v, seqlens=None)``,
+    ``forward_partial`` and ``combine``.  Replaces the reference's JIT-built
+    module (attention_decode/__init__.py:8-23, csrc/binding.cpp:3-8); there
+    is no fallback if it is missing."""
+    _torch()
     _lib.load_library()
-    return _Extension()
+    try:
+        from . import adb_torch_ext
+    except ImportError as exc:
+        raise ImportError(
+            "attention_decode/adb_torch_ext.so is missing or does not load: build it with "
+            "`python -c 'import __graft_entry__ as g; g.build()'` from the repository root"
+        ) from exc
+    return adb_torch_ext

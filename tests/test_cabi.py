@@ -138,13 +138,12 @@ def test_append_arguments_are_checked_on_host():
 
 def test_extension_object_has_the_reference_method_and_the_additions():
     """attention_decode/__init__.py:8-23 binds `forward`; the additions keep it."""
-    import inspect
-
     import attention_decode
     from attention_decode import sharded
 
     ext = attention_decode._get_extension()
-    assert list(inspect.signature(ext.forward).parameters)[:3] == ["q", "k", "v"]
+    # a pybind function: its signature is the first line of its docstring
+    assert ext.forward.__doc__.startswith("forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor")
     assert callable(ext.forward_partial) and callable(ext.combine)
     assert sharded.attention_decode_sharded is sharded.attention_decode_sequence_sharded
 
