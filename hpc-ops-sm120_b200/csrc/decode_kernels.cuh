@@ -1366,8 +1366,8 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
         if constexpr (kFp8) {
           // one 16-byte chunk of an FP8 row is a 16-dim slab: an x4 load
           // covers slabs 2*s2 and 2*s2 + 1 of 16 tokens; each register holds
-          // 4 dims of one token, turned into two f16 pairs (values * 2^-8;
-          // the host folds 2^8 into the K and V scales)
+          // 4 dims of one token, turned into two f16 pairs (exact values;
+          // the K and V scales are applied to the scores and the output)
 #pragma unroll
           for (int s2 = 0; s2 < kSlabs / 2; ++s2) {
             uint32_t r[4];

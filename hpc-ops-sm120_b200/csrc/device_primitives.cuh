@@ -183,23 +183,22 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// Two e4m3 values to an f16x2 register holding them times 2^-8, exactly,
-// with integer operations only.  f16's exponent bias (15) exceeds e4m3's (7)
-// by 8 and both formats become subnormal at exponent field 0, so moving an
-// e4m3 byte's sign to bit 15 and its exponent and mantissa (bits 6..0) to
-// bits 13..7 gives the f16 of value * 2^-8 for every finite code (the NaN
-// code S.1111.111 becomes a finite number).  `w` holds the two bytes at
-// byte positions 1 and 3 (the low and high halves' top bytes).
-__device__ __forceinline__ uint32_t e4m3_pair_to_f16x2_scaled(uint32_t w) {
-  return (w & 0x80008000u) | ((w >> 1) & 0x3F803F80u);
+// Two e4m3 values (the low and high byte of `pair`) to an f16x2 register
+// (low half from the low byte), exactly: every e4m3 value is an f16 value
+// (cvt.rn.f16x2.e4m3x2, PTX ISA, sm_89 and later; the NaN code stays NaN).
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t pair) {
+  uint32_t out;
+  const uint16_t lo16 = static_cast<uint16_t>(pair);
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(out) : "h"(lo16));
+  return out;
 }
 
-// Pairs of the four e4m3 bytes (b0, b1, b2, b3) of x, as f16x2 times 2^-8:
+// Pairs of the four e4m3 bytes (b0, b1, b2, b3) of x as f16x2:
 // (b0, b1), (b2, b3) -- consecutive elements -- and (b0, b2), (b1, b3).
-__device__ __forceinline__ uint32_t e4m3_01(uint32_t x) { return e4m3_pair_to_f16x2_scaled(__byte_perm(x, 0u, 0x1404u)); }
-__device__ __forceinline__ uint32_t e4m3_23(uint32_t x) { return e4m3_pair_to_f16x2_scaled(__byte_perm(x, 0u, 0x3424u)); }
-__device__ __forceinline__ uint32_t e4m3_02(uint32_t x) { return e4m3_pair_to_f16x2_scaled(__byte_perm(x, 0u, 0x2404u)); }
-__device__ __forceinline__ uint32_t e4m3_13(uint32_t x) { return e4m3_pair_to_f16x2_scaled(__byte_perm(x, 0u, 0x3414u)); }
+__device__ __forceinline__ uint32_t e4m3_01(uint32_t x) { return e4m3x2_to_f16x2(x); }
+__device__ __forceinline__ uint32_t e4m3_23(uint32_t x) { return e4m3x2_to_f16x2(x >> 16); }
+__device__ __forceinline__ uint32_t e4m3_02(uint32_t x) { return e4m3x2_to_f16x2(__byte_perm(x, 0u, 0x0020u)); }
+__device__ __forceinline__ uint32_t e4m3_13(uint32_t x) { return e4m3x2_to_f16x2(__byte_perm(x, 0u, 0x0031u)); }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
