@@ -598,7 +598,9 @@ std::mutex g_fixed_mutex;
 void* g_fixed_address[kMaxDevices] = {};
 
 // Device address of g_adb_fixed_workspace on `device`, which must be the
-// current device; looked up on the first call per device and kept.
+// current device; looked up on the first call per device and kept (so it is
+// stale after cudaDeviceReset reloads the module: the header says not to
+// call the entry point again in that process).
 int fixed_workspace(int device, void** address) {
   std::lock_guard<std::mutex> lock(g_fixed_mutex);
   if (g_fixed_address[device] == nullptr) {

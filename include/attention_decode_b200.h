@@ -181,11 +181,20 @@ ADB_API int adb_decode_paged(const void* q, const void* k_cache, const void* v_c
  *
  * Limits and behaviour:
  *  - problems whose scratch would exceed ADB_NO_ALLOC_WORKSPACE_BYTES are
- *    rejected with ADB_ERR_WORKSPACE (roughly (148 + batch*kv_heads) *
- *    group * head_dim * 4 bytes must fit; no work stealing is used here);
+ *    rejected with ADB_ERR_WORKSPACE.  No work stealing is used here, so the
+ *    scratch is exactly: a header of 8*ctas + 8 + 8*batch*kv_heads bytes,
+ *    then slots = ctas + batch*kv_heads segment states of group*head_dim
+ *    and group*2 floats, each of the three parts rounded up to 256 bytes,
+ *    where ctas = min(SM count, batch*kv_heads*ceil(kv_len/tile)) and tile
+ *    is 128 tokens (64 when that product is below twice the SM count).
+ *    About (148 + batch*kv_heads) * group * (head_dim + 2) * 4 bytes on a
+ *    B200; adb_decode_workspace_size gives an upper bound (it also counts
+ *    the slots work stealing may use);
  *  - the first call on a device looks up the array's device address
- *    (cudaGetSymbolAddress) with that device current; make that first call
- *    before any stream capture;
+ *    (cudaGetSymbolAddress) with that device current and keeps it; make that
+ *    first call before any stream capture.  The kept address is invalid
+ *    after cudaDeviceReset (or any teardown of the device's primary
+ *    context): do not call this entry point again in that process;
  *  - every call uses the same array, and its scheduler header is cleared with
  *    one cudaMemsetAsync on `stream` before the kernel, so calls that overlap
  *    on the GPU (different streams, or different host threads) race and

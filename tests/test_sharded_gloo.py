@@ -134,10 +134,6 @@ def test_batch_shard_slices_cover_the_batch():
         assert covered == list(range(batch))
 
 
-if __name__ == "__main__":
-    sys.exit(pytest.main([__file__, "-q"]))
-
-
 def test_batch_shards_of_baseline_inputs_reproduce_the_full_batch():
     """A rank's share of one global batch (slice or token-balanced index list)
     holds exactly the full batch's rows, so strong scaling shards one problem."""
@@ -150,3 +146,7 @@ def test_batch_shards_of_baseline_inputs_reproduce_the_full_batch():
         qs, ks, vs, ls = cfg.make_inputs("cpu", seed=11, batch_slice=part)
         assert torch.equal(qs, q[part]) and torch.equal(ks, k[part]) and torch.equal(vs, v[part])
         assert torch.equal(ls, lens[part])
+
+
+if __name__ == "__main__":
+    sys.exit(pytest.main([__file__, "-q"]))
