@@ -181,9 +181,11 @@ def _launch(q, k, v, seqlens, out=None, acc=None, ml=None):
     _lib.check(lib, status)
 
 
-def _launch_exchange(q, k, v, seqlens, bases, rank: int):
+def _launch_exchange(q, k, v, seqlens, bases, rank: int, out=None, timeout_us: int = 0):
     """adb_decode_exchange: partial decode whose states go to slot `rank` of
-    every exchange buffer in `bases` (device addresses as mapped here)."""
+    every exchange buffer in `bases` (device addresses as mapped here).  With
+    `out`, adb_decode_exchange_merged: the same launch also waits for every
+    rank's states and merges them into `out` (ranks on distinct GPUs only)."""
     torch = _torch()
     lib = _lib.load_library()
     batch, q_heads, _, head_dim = q.shape
@@ -194,6 +196,16 @@ def _launch_exchange(q, k, v, seqlens, bases, rank: int):
     workspace, flags = _workspace(q.device, device, stream, nbytes, header)
     lens = seqlens.data_ptr() if seqlens is not None else None
     array = (ctypes.c_void_p * len(bases))(*bases)
+    if out is not None:
+        _lib.check(
+            lib,
+            lib.adb_decode_exchange_merged(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), lens, batch, q_heads, kv_heads, kv_len, head_dim,
+                array, len(bases), rank, out.data_ptr(), timeout_us, workspace.data_ptr(), workspace.numel(),
+                flags, device, stream,
+            ),
+        )
+        return
     _lib.check(
         lib,
         lib.adb_decode_exchange(

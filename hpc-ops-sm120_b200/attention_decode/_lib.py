@@ -93,6 +93,11 @@ PROTOTYPES = {
          _vp, ctypes.c_size_t, ctypes.c_uint, _int, _vp],
     ),
     "adb_exchange_merge": (_int, [_vp, _int, _i64, _i64, _vp, _i64, _int, _vp]),
+    "adb_decode_exchange_merged": (
+        _int,
+        [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_vp), _int, _int,
+         _vp, _i64, _vp, ctypes.c_size_t, ctypes.c_uint, _int, _vp],
+    ),
     "adb_read_error_flag": (_int, [_int, ctypes.POINTER(_int), _int]),
     "adb_launch_count": (_int, [ctypes.POINTER(_i64)]),
     "adb_timing_enable": (_int, [_int]),

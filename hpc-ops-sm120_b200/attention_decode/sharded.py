@@ -29,6 +29,7 @@ from __future__ import annotations
 
 import ctypes
 import heapq
+import socket
 
 import torch
 
@@ -97,6 +98,7 @@ class PeerExchange:
         if _world is not None:  # single-process emulation (see `emulated`)
             self.dist, self.world, self.rank = None, _world, None
             self.bases = [self._alloc() for _ in range(_world)]
+            self.fused = False  # the emulated ranks share one GPU
             return
         import torch.distributed as dist
 
@@ -107,6 +109,14 @@ class PeerExchange:
         _lib.check(self.lib, self.lib.adb_ipc_handle(mine, self.index, handle))
         handles = [None] * self.world
         dist.all_gather_object(handles, handle.raw, group=group)
+        # The fused step (decode and merge in one launch) makes each rank's
+        # kernel wait for the others' kernels, so it is used only when every
+        # rank has a GPU of its own.
+        props = torch.cuda.get_device_properties(self.device)
+        where = (socket.gethostname(), props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+        places = [None] * self.world
+        dist.all_gather_object(places, where, group=group)
+        self.fused = len(set(places)) == self.world
         self.bases = []
         for r, raw in enumerate(handles):
             if r == self.rank:
@@ -135,6 +145,17 @@ class PeerExchange:
     def decode(self, q, k, v, rank: int | None = None, seqlens=None):
         """This rank's partial decode; its states go to every rank's buffer."""
         _launch_exchange(q, k, v, seqlens, self.bases, self.rank if rank is None else rank)
+
+    def decode_merged(self, q, k, v, out, seqlens=None, timeout_s: float = DEFAULT_PEER_TIMEOUT_S):
+        """decode + merge in one launch (adb_decode_exchange_merged): this
+        rank's states go to every buffer and the merged rows to `out`.  Only
+        when ``self.fused`` (every rank on its own GPU)."""
+        if not self.fused:
+            raise RuntimeError("decode_merged needs every rank on a GPU of its own (use decode + merge)")
+        if out.dtype != torch.bfloat16 or not out.is_contiguous() or out.numel() != self.rows * self.head_dim:
+            raise ValueError("out must be a contiguous bf16 buffer of rows * head_dim elements")
+        _launch_exchange(q, k, v, seqlens, self.bases, self.rank, out=out, timeout_us=max(1, int(timeout_s * 1e6)))
+        return out
 
     def merge(self, out, rank: int | None = None, timeout_s: float = DEFAULT_PEER_TIMEOUT_S):
         """Wait for every rank's states of this call (bounded) and merge them
@@ -179,7 +200,7 @@ class SequenceShardedDecode:
     host is the bottleneck."""
 
     def __init__(self, q, k_local, v_local, group=None, seqlens_local=None, transport: str = "p2p",
-                 timeout_s: float = DEFAULT_PEER_TIMEOUT_S):
+                 timeout_s: float = DEFAULT_PEER_TIMEOUT_S, fused: bool | None = None):
         import torch.distributed as dist
 
         if transport not in ("p2p", "nccl"):
@@ -197,8 +218,10 @@ class SequenceShardedDecode:
         self.graph = None
         self.exchange = None
         self.buf = self.gathered = None
+        self.fused = False
         if transport == "p2p":
             self.exchange = PeerExchange(self.rows, head_dim, group, q.device)
+            self.fused = self.exchange.fused if fused is None else (bool(fused) and self.exchange.fused)
             return
         block, ml_off = state_layout(self.rows, head_dim)
         self.buf = torch.empty(block, dtype=torch.float32, device=q.device)
@@ -223,8 +246,11 @@ class SequenceShardedDecode:
 
     def run(self, q):
         if self.exchange is not None:
-            self.exchange.decode(q, self.k, self.v, seqlens=self.seqlens)
-            self.exchange.merge(self.out, timeout_s=self.timeout_s)
+            if self.fused:
+                self.exchange.decode_merged(q, self.k, self.v, self.out, seqlens=self.seqlens, timeout_s=self.timeout_s)
+            else:
+                self.exchange.decode(q, self.k, self.v, seqlens=self.seqlens)
+                self.exchange.merge(self.out, timeout_s=self.timeout_s)
             return self.out.view(self.shape)
         attention_decode_partial(q, self.k, self.v, self.seqlens, out_acc=self.acc, out_ml=self.ml)
         self.dist.all_gather_into_tensor(self.gathered, self.buf, group=self.group)

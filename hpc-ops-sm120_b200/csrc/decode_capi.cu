@@ -431,6 +431,8 @@ struct ExchangeArgs {
   uint8_t* base[adb::kMaxRanks];
   int world;
   int rank;
+  void* out = nullptr;      // fused merge: BF16 [rows][D] (nullptr: states only)
+  int64_t timeout_us = 0;   // fused merge: bound of the wait for the peers' flags
 };
 
 int run_decode(const void* q, const void* k, const void* v, const int32_t* seqlens, void* out,
@@ -542,10 +544,21 @@ int run_decode(const void* q, const void* k, const void* v, const int32_t* seqle
   for (int r = 0; r < adb::kMaxRanks; ++r) p.x_base[r] = nullptr;
   p.x_world = 0;
   p.x_rank = 0;
+  p.x_out = nullptr;
+  p.x_mergers = 0;
+  p.x_timeout_ns = 0;
   if (exchange != nullptr) {
     for (int r = 0; r < exchange->world; ++r) p.x_base[r] = exchange->base[r];
     p.x_world = exchange->world;
     p.x_rank = exchange->rank;
+    if (exchange->out != nullptr) {
+      // one warp per row over the first CTAs: rows / 4 mergers at most
+      const int64_t rows = s.B * s.Hq;
+      const int64_t mergers = (rows + 3) / 4;
+      p.x_out = static_cast<__nv_bfloat16*>(exchange->out);
+      p.x_mergers = static_cast<int>(mergers < plan.num_ctas ? mergers : plan.num_ctas);
+      p.x_timeout_ns = static_cast<uint64_t>(exchange->timeout_us) * 1000ull;
+    }
   }
 
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
@@ -894,6 +907,33 @@ int adb_decode_exchange(const void* q, const void* k, const void* v, const int32
                     head_dim, workspace, workspace_bytes, flags, device, stream, true, &x);
 }
 
+int adb_decode_exchange_merged(const void* q, const void* k, const void* v, const int32_t* seqlens,
+                               int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t kv_len,
+                               int64_t head_dim, void* const* exchange, int world, int rank, void* out,
+                               int64_t timeout_us, void* workspace, size_t workspace_bytes,
+                               unsigned flags, int device, void* stream) {
+  if (exchange == nullptr || out == nullptr)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "exchange array and output pointer must be non-null");
+  if (world < 1 || world > adb::kMaxRanks)
+    return fail(ADB_ERR_UNSUPPORTED, "world size must be 1..%d (got %d)", adb::kMaxRanks, world);
+  if (rank < 0 || rank >= world)
+    return fail(ADB_ERR_INVALID_ARGUMENT, "rank %d is outside 0..%d", rank, world - 1);
+  if (timeout_us <= 0) return fail(ADB_ERR_INVALID_ARGUMENT, "timeout must be positive");
+  ExchangeArgs x;
+  for (int r = 0; r < adb::kMaxRanks; ++r) x.base[r] = nullptr;
+  for (int r = 0; r < world; ++r) {
+    if (exchange[r] == nullptr || !is_aligned(exchange[r], 256))
+      return fail(ADB_ERR_INVALID_ARGUMENT, "exchange buffer of rank %d is null or misaligned", r);
+    x.base[r] = static_cast<uint8_t*>(exchange[r]);
+  }
+  x.world = world;
+  x.rank = rank;
+  x.out = out;
+  x.timeout_us = timeout_us;
+  return run_decode(q, k, v, seqlens, nullptr, nullptr, nullptr, batch, q_heads, kv_heads, kv_len,
+                    head_dim, workspace, workspace_bytes, flags, device, stream, true, &x);
+}
+
 int adb_exchange_merge(const void* exchange, int world, int64_t rows, int64_t head_dim, void* out,
                        int64_t timeout_us, int device, void* stream) {
   if (exchange == nullptr || out == nullptr)
@@ -973,10 +1013,13 @@ __attribute__((visibility("default"))) int adb_trace_read(unsigned long long* ho
   return static_cast<int>(next & 1u);
 }
 
-// Diagnostic build only: the per-launch log (256 x 2 u64) and the number of
+// Diagnostic build only: the per-launch log (256 x 4 u64, then the merge log
+// 256 x 3 u64) and the number of
 // launches so far.
 __attribute__((visibility("default"))) int adb_launch_log_read(unsigned long long* host, unsigned* launches) {
-  cudaError_t e = cudaMemcpyFromSymbol(host, adb::g_adb_launch_log, sizeof(unsigned long long) * 512);
+  cudaError_t e = cudaMemcpyFromSymbol(host, adb::g_adb_launch_log, sizeof(unsigned long long) * 1024);
+  if (e == cudaSuccess)
+    e = cudaMemcpyFromSymbol(host + 1024, adb::g_adb_merge_log, sizeof(unsigned long long) * 768);
   if (e == cudaSuccess) e = cudaMemcpyFromSymbol(launches, adb::g_adb_trace_launch, sizeof(unsigned));
   if (e != cudaSuccess) return cuda_fail(e, "reading the launch log");
   return ADB_OK;

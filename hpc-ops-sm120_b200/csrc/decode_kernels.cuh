@@ -79,8 +79,11 @@ constexpr int kTraceCtas = 1024;
 __device__ unsigned long long g_adb_trace[2][kTraceCtas][16];
 __device__ unsigned int g_adb_trace_launch = 0;
 // Per launch (ring of 256): [0] earliest return from the grid dependency wait,
-// [1] exit of the last CTA.
-__device__ unsigned long long g_adb_launch_log[256][2];
+// [1] exit of the last CTA, [2] / [3] before the exchange publication's
+// system fence / after its flag stores.  Per exchange merge (by call number):
+// [0] after the grid dependency wait, [1] all flags seen, [2] CTA 0 done.
+__device__ unsigned long long g_adb_launch_log[256][4];
+__device__ unsigned long long g_adb_merge_log[256][3];
 #define ADB_TRACE_ONLY(...) __VA_ARGS__
 #else
 #define ADB_TRACE_ONLY(...)
@@ -170,6 +173,12 @@ struct DecodeParams {
   uint8_t* x_base[kMaxRanks];  // each rank's exchange buffer as mapped here
   int x_world;
   int x_rank;
+  // Fused merge (x_mergers > 0, ranks on distinct GPUs only): CTAs
+  // 0..x_mergers-1 wait, bounded by x_timeout_ns, for every rank's flag of
+  // this call and merge the rows into x_out (no separate merge launch).
+  __nv_bfloat16* x_out;
+  int x_mergers;
+  uint64_t x_timeout_ns;
 };
 
 // Number of copies of each partial state a decode stores (one per rank).
@@ -202,6 +211,63 @@ __device__ __forceinline__ float* partial_ml(const DecodeParams& p, int s, int64
 }
 
 __device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
+
+// Merges parts <= kMaxRanks partial states (m in natural units) of one row
+// into BF16; called by one warp.  Every part's (m, l) and accumulator row are
+// requested together (lane r reads part r's (m, l); each lane its dims of
+// every part), so the merge is one round trip of loads.  Empty parts (l = 0)
+// weigh zero.  The cross-GPU merge of sequence shards (the reference's
+// merge_splits, csrc/decode.cu:169-184, over ranks).
+template <int D>
+__device__ __forceinline__ void merge_row_few(const float* __restrict__ acc, int64_t acc_stride,
+                                              const float* __restrict__ ml, int64_t ml_stride,
+                                              int parts, int64_t row, __nv_bfloat16* __restrict__ out,
+                                              int lane) {
+  constexpr int kPer = D / 32;
+  constexpr float kLog2e = 1.4426950408889634f;
+  float m = neg_inf(), l = 0.f;
+  if (lane < parts) {
+    const float2 v = __ldcg(reinterpret_cast<const float2*>(ml + lane * ml_stride + 2 * row));
+    m = v.x;
+    l = v.y;
+  }
+  float x[kMaxRanks][kPer];
+#pragma unroll
+  for (int r = 0; r < kMaxRanks; ++r) {
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) x[r][i] = 0.f;
+    if (r < parts) {
+      const float* src = acc + r * acc_stride + row * D + lane * kPer;
+      if constexpr (kPer == 4) {
+        const float4 v4 = __ldcg(reinterpret_cast<const float4*>(src));
+        x[r][0] = v4.x; x[r][1] = v4.y; x[r][2] = v4.z; x[r][3] = v4.w;
+      } else {
+        const float2 v2 = __ldcg(reinterpret_cast<const float2*>(src));
+        x[r][0] = v2.x; x[r][1] = v2.y;
+      }
+    }
+  }
+  float M = l > 0.f ? m : neg_inf();
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  const float Mu = M == neg_inf() ? 0.f : M;
+  const float w = l > 0.f ? fast_exp2((m - Mu) * kLog2e) : 0.f;
+  float L = w * l;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  float O[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) O[i] = 0.f;
+#pragma unroll
+  for (int r = 0; r < kMaxRanks; ++r) {
+    const float wr = __shfl_sync(0xffffffffu, w, r);
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) O[i] += wr > 0.f ? wr * x[r][i] : 0.f;
+  }
+  __nv_bfloat16* dst = out + row * D + lane * kPer;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) dst[i] = __float2bfloat16_rn(L > 0.f ? O[i] / L : 0.f);
+}
 
 __device__ __forceinline__ int32_t clamped_len(const DecodeParams& p, int64_t b) {
   if (p.seqlens == nullptr) return static_cast<int32_t>(p.kv_len);
@@ -427,7 +493,8 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   // misc[0..32]: scan scratch; misc[40..43]: batches / bases of the first and
   // last tile; misc[44]: dynamic slot of a thief flush; misc[46]: broadcast
   // flag; misc[47]: dynamic slots in use; misc[48]: merge segment count;
-  // misc[50]: abort flag; misc[52]: parity of the exchange slots written
+  // misc[50]: abort flag; misc[52] / misc[53]: parity of the exchange slots
+  // written / this call's number; misc[54]: peers' flags seen (fused merge)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 50);
   // merge slot list, aliased on fl_acc (see StreamCfg)
   int32_t* mg_list = reinterpret_cast<int32_t*>(fl_acc);
@@ -522,9 +589,16 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   // Partial-state stores go to the local arrays, or (peer exchange) to this
   // rank's slot in every rank's exchange buffer, at the parity of the call
   // being produced (read once here and kept in shared memory, misc[52]).
+  // Only the consumer warps wait for that read (they wait for the first tile
+  // anyway); the producer goes straight to its first loads.  The varlen
+  // set-up below passes __syncthreads before any thread uses the value.
   if constexpr (kExchange) {
-    if (tid == 0) misc[52] = (x_epoch(p) + 1u) & 1u;
-    __syncthreads();
+    if (tid == 0) {
+      const uint32_t call = x_epoch(p) + 1u;  // the call this launch produces
+      misc[52] = call & 1u;
+      misc[53] = call;
+    }
+    if (warp < kWarps) named_barrier_sync(1, C::kConsumerThreads);
   }
   auto acc_dest = [&](int s) -> float* {
     return partial_acc<kExchange>(p, s, kExchange ? misc[52] : 0, P * G, D);
@@ -1533,12 +1607,57 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       g_adb_trace_launch += 1u;
 #endif
       if constexpr (kExchange) {
-        __threadfence_system();
+        ADB_TRACE_ONLY(const unsigned tr_l = (g_adb_trace_launch - 1u) & 255u; g_adb_launch_log[tr_l][2] = global_timer_ns();)
+        fence_acq_rel_sys();
         const uint32_t call = x_epoch(p) + 1u;
         for (int s = 0; s < p.x_world; ++s)
           st_release_sys_u32(
               reinterpret_cast<uint32_t*>(p.x_base[s] + kXFlagsOffset) + p.x_rank, call);
         *reinterpret_cast<volatile uint32_t*>(p.x_base[p.x_rank] + kXEpochOffset) = call;
+        ADB_TRACE_ONLY(g_adb_launch_log[tr_l][3] = global_timer_ns();)
+      }
+    }
+  }
+  // Fused merge: CTAs 0..x_mergers-1 (each a share of the rows) wait for
+  // every rank's flag of this call in this rank's buffer -- this rank's own
+  // flag is raised by its last CTA above -- and merge the `world` states of
+  // each row.  Ranks run on distinct GPUs (the host guarantees it), and every
+  // CTA of this persistent grid is resident, so each wait ends; it is also
+  // bounded by x_timeout_ns (zero rows and the device error bit after it).
+  if constexpr (kExchange) {
+    if (p.x_mergers > 0 && c < p.x_mergers) {
+      const uint32_t call = static_cast<uint32_t>(misc[53]);
+      const uint8_t* xbuf = p.x_base[p.x_rank];
+      if (tid == 0) {
+        const uint32_t* flags = reinterpret_cast<const uint32_t*>(xbuf + kXFlagsOffset);
+        int ok = 1;
+        const uint64_t start = global_timer_ns();
+        for (int s = 0; s < p.x_world && ok; ++s) {
+          // flags only grow; a rank one call ahead has already passed `call`
+          while (static_cast<int32_t>(ld_acquire_sys_u32(flags + s) - call) < 0) {
+            if (global_timer_ns() - start > p.x_timeout_ns) {
+              ok = 0;
+              atomicOr(&g_adb_error_flag, kErrPeerTimeout);
+              break;
+            }
+            __nanosleep(32);
+          }
+        }
+        misc[54] = ok;
+      }
+      bar();
+      const int64_t rows = P * G;
+      const int64_t r0 = c * rows / p.x_mergers, r1 = (c + 1) * rows / p.x_mergers;
+      const int64_t par = call & 1u;
+      const float* xacc = reinterpret_cast<const float*>(xbuf + kXAccOffset) + par * p.x_world * rows * D;
+      const float* xml = reinterpret_cast<const float*>(xbuf + x_ml_offset(p.x_world, rows, D)) +
+                         par * p.x_world * rows * 2;
+      for (int64_t row = r0 + warp; row < r1; row += kWarps) {
+        if (misc[54]) {
+          merge_row_few<D>(xacc, rows * D, xml, rows * 2, p.x_world, row, p.x_out, lane);
+        } else {
+          for (int d = lane; d < D; d += 32) p.x_out[row * D + d] = __float2bfloat16_rn(0.f);
+        }
       }
     }
   }
@@ -1586,7 +1705,10 @@ __global__ void __launch_bounds__(256)
                         int64_t rows, __nv_bfloat16* __restrict__ out) {
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
-  merge_row<D>(acc, acc_stride, ml, ml_stride, parts, row, out, threadIdx.x & 31);
+  if (parts <= kMaxRanks)
+    merge_row_few<D>(acc, acc_stride, ml, ml_stride, static_cast<int>(parts), row, out, threadIdx.x & 31);
+  else
+    merge_row<D>(acc, acc_stride, ml, ml_stride, parts, row, out, threadIdx.x & 31);
 }
 
 // The merge step of a peer exchange (see the layout above), on one rank:
@@ -1604,6 +1726,7 @@ __global__ void __launch_bounds__(256)
   griddep_wait();
   __shared__ int ready;
   const uint32_t call = *reinterpret_cast<const volatile uint32_t*>(xbuf + kXEpochOffset);
+  ADB_TRACE_ONLY(if (blockIdx.x == 0 && threadIdx.x == 0) g_adb_merge_log[call & 255u][0] = global_timer_ns();)
   if (threadIdx.x == 0) {
     const uint32_t* flags = reinterpret_cast<const uint32_t*>(xbuf + kXFlagsOffset);
     int ok = 1;
@@ -1620,6 +1743,7 @@ __global__ void __launch_bounds__(256)
       }
     }
     ready = ok;
+    ADB_TRACE_ONLY(if (blockIdx.x == 0) g_adb_merge_log[call & 255u][1] = global_timer_ns();)
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
@@ -1632,7 +1756,8 @@ __global__ void __launch_bounds__(256)
   const int64_t par = call & 1u;
   const float* acc = reinterpret_cast<const float*>(xbuf + kXAccOffset) + par * world * rows * D;
   const float* ml = reinterpret_cast<const float*>(xbuf + x_ml_offset(world, rows, D)) + par * world * rows * 2;
-  merge_row<D>(acc, rows * D, ml, rows * 2, world, row, out, lane);
+  merge_row_few<D>(acc, rows * D, ml, rows * 2, world, row, out, lane);
+  ADB_TRACE_ONLY(if (blockIdx.x == 0 && threadIdx.x == 0) g_adb_merge_log[call & 255u][2] = global_timer_ns();)
 }
 
 }  // namespace adb

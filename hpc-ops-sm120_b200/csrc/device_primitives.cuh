@@ -229,6 +229,13 @@ __device__ __forceinline__ void st_release_sys_u32(uint32_t* ptr, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }
 
+// Release/acquire fence at system scope (orders this thread's, and by
+// cumulativity everything it has observed, earlier memory accesses before
+// its later ones for observers on other GPUs); lighter than fence.sc.sys.
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* ptr) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");

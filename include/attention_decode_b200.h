@@ -278,6 +278,21 @@ ADB_API int adb_decode_exchange(const void* q, const void* k, const void* v,
 ADB_API int adb_exchange_merge(const void* exchange, int world, int64_t rows, int64_t head_dim,
                                void* out, int64_t timeout_us, int device, void* stream);
 
+/* adb_decode_exchange and adb_exchange_merge in ONE launch: after this rank's
+ * states are published, the kernel's first CTAs wait (bounded by
+ * `timeout_us`) for every rank's flag of the call and merge the rows into
+ * `out` [batch * q_heads, head_dim] BF16, with no second kernel and no grid
+ * boundary between the exchange and the merge.  Only for ranks that run on
+ * DISTINCT GPUs: each rank's kernel waits for the others' kernels, so two
+ * ranks sharing a GPU must use the two-call form.  Same errors and timeout
+ * behaviour as the pair it replaces. */
+ADB_API int adb_decode_exchange_merged(const void* q, const void* k, const void* v,
+                                       const int32_t* seqlens, int64_t batch, int64_t q_heads,
+                                       int64_t kv_heads, int64_t kv_len, int64_t head_dim,
+                                       void* const* exchange, int world, int rank, void* out,
+                                       int64_t timeout_us, void* workspace, size_t workspace_bytes,
+                                       unsigned flags, int device, void* stream);
+
 /* Reads (and optionally clears) the sticky device error word that kernels
  * set when a bounded wait gives up; 0 means no kernel has reported an
  * error on `device`.  Synchronous (a device-to-host copy); for diagnostics. */

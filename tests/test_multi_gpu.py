@@ -1,6 +1,7 @@
 """Multi-GPU decode: sequence sharding (partial states exchanged through
-NVLink peer memory by the decode kernel itself, and through an NCCL
-all_gather; merged on every rank, eagerly and replayed from a CUDA graph) and
+NVLink peer memory by the decode kernel itself -- merged in the same launch,
+or by a second kernel -- and through an NCCL all_gather; merged on every
+rank, eagerly and replayed from a CUDA graph) and
 batch sharding (no collective).  Needs at least two GPUs; ranks are spawned
 processes, one per GPU, with a short process-group timeout so that a failure
 ends in an error, not a hang."""
@@ -46,10 +47,15 @@ def _worker(rank, world, port, results):
         expected = oracle_reference(q, k, v) if rank == 0 else None
         q2 = inputs(device, 1, 128, 8, batch=1, hq=64, seed=93)[0]
         full2 = ad.attention_decode(q2, k, v)
-        for transport in ("p2p", "nccl"):
+        # p2p fused (decode and merge in one launch, the default on distinct
+        # GPUs), p2p in two launches, and NCCL
+        for transport, fused in (("p2p", None), ("p2p", False), ("nccl", None)):
             step = sharded.SequenceShardedDecode(
-                q.clone(), k[:, :, lo:hi].contiguous(), v[:, :, lo:hi].contiguous(), transport=transport
+                q.clone(), k[:, :, lo:hi].contiguous(), v[:, :, lo:hi].contiguous(), transport=transport,
+                fused=fused,
             )
+            if transport == "p2p":
+                assert step.fused == (fused is None)
             out = step().clone()
             again = step().clone()
             torch.cuda.synchronize(device)

@@ -136,3 +136,49 @@ def test_missing_peer_ends_the_wait_with_an_error(device):
         check(full, oracle_reference(q, k, v), q)
     finally:
         exchange.close()
+
+
+def test_fused_merge_without_peers_times_out_with_error(device):
+    """The fused decode + merge (adb_decode_exchange_merged) of rank 0 of a
+    2-rank world whose rank 1 never runs: its merging CTAs wait for a flag
+    that nothing sets, give up after the 20 ms limit, write zero rows and set
+    the peer-timeout bit; the context stays usable.  (Only rank 0 launches,
+    so no kernel waits on another one on this GPU.)"""
+    import attention_decode
+
+    world, S, dim, hq, hkv = 2, 1024, 64, 32, 8
+    q, k, v = inputs(device, S, dim, hkv, hq=hq, seed=333)
+    shards = _shard(k, v, world)
+    exchange = sharded.PeerExchange.emulated(world, hq, dim, device)
+    try:
+        ad.read_error_flag(device.index or 0)  # clear
+        out = torch.full((hq, dim), 7.0, dtype=torch.bfloat16, device=device)
+        attention_decode._launch_exchange(q, *shards[0], None, exchange.bases, 0, out=out, timeout_us=20000)
+        torch.cuda.synchronize(device)
+        flag = ad.read_error_flag(device.index or 0)
+        assert flag & _lib.ADB_ERROR_FLAG_PEER_TIMEOUT
+        assert torch.count_nonzero(out).item() == 0
+        full = ad.attention_decode(q, k, v)
+        check(full, oracle_reference(q, k, v), q)
+    finally:
+        exchange.close()
+
+
+def test_fused_merge_of_a_single_rank_equals_the_decode(device):
+    """World of one: the fused launch publishes its own flag and merges its
+    own state (no waiting on anything else), which must equal the plain
+    decode."""
+    import attention_decode
+
+    S, dim, hq, hkv = 4099, 128, 64, 8
+    q, k, v = inputs(device, S, dim, hkv, hq=hq, seed=334)
+    exchange = sharded.PeerExchange.emulated(1, hq, dim, device)
+    try:
+        for _ in range(3):  # both parities
+            out = torch.full((hq, dim), float("nan"), dtype=torch.bfloat16, device=device)
+            attention_decode._launch_exchange(q, k, v, None, exchange.bases, 0, out=out, timeout_us=2_000_000)
+            torch.cuda.synchronize(device)
+            check(out.view(q.shape), oracle_reference(q, k, v), q)
+        assert ad.read_error_flag(device.index or 0) == 0
+    finally:
+        exchange.close()
