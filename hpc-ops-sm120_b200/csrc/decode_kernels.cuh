@@ -1045,7 +1045,7 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       bar();
       const int n = static_cast<int>(misc[48]);
       constexpr int H = C::kHeadsPerWarp;
-      constexpr int kU = 4;  // segments whose rows are in flight together
+      constexpr int kU = 8;  // segments whose rows are in flight together
       for (int c0 = 0; c0 < n; c0 += 32) {
         const int cn = n - c0 < 32 ? n - c0 : 32;
         // Lane j holds segment c0 + j's (m, l) of each of this warp's heads:
