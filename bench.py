@@ -108,7 +108,14 @@ def profile_traffic(kernel_key: str):
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clock/throttle samples taken while the timed region runs."""
+    """Clock/throttle samples around the timed region: nvidia-smi every 100 ms
+    (the recipe's query) and, where the NVML bindings load, a thread reading
+    the SM clock, the clock-event reasons and the power every ~2 ms (read-only
+    queries), so that even a timed region of a few ms has samples inside it.
+    ``mark_start``/``mark_stop`` bracket the timed region on the host."""
+
+    NVML_REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+                    ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4))
 
     FIELDS = (
         "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -120,13 +127,42 @@ class ClockSampler:
         self.proc = None
         self.lines: list[str] = []
         self.target = None
+        self.fast: list[tuple] = []  # (host time, sm MHz, reasons bitmask, power W)
+        self.window = [None, None]
+        self._stop_fast = threading.Event()
+        self._fast_thread = None
         try:
             props = torch.cuda.get_device_properties(device)
             self.target = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
         except Exception:
             self.target = None
 
+    def _fast_loop(self, handle, nvml):
+        while not self._stop_fast.is_set():
+            try:
+                self.fast.append((time.perf_counter(), nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM),
+                                  nvml.nvmlDeviceGetCurrentClocksEventReasons(handle),
+                                  nvml.nvmlDeviceGetPowerUsage(handle) / 1000.0))
+            except Exception:
+                return
+            time.sleep(0.002)
+
+    def mark_start(self):
+        self.window[0] = time.perf_counter()
+
+    def mark_stop(self):
+        self.window[1] = time.perf_counter()
+
     def start(self):
+        try:
+            import pynvml as nvml
+
+            nvml.nvmlInit()
+            handle = nvml.nvmlDeviceGetHandleByPciBusId(self.target) if self.target else nvml.nvmlDeviceGetHandleByIndex(0)
+            self._fast_thread = threading.Thread(target=self._fast_loop, args=(handle, nvml), daemon=True)
+            self._fast_thread.start()
+        except Exception:
+            self._fast_thread = None
         cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"]
         if self.target:
             cmd += ["-i", self.target]
@@ -142,9 +178,25 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def _fast_summary(self):
+        self._stop_fast.set()
+        if self._fast_thread is not None:
+            self._fast_thread.join(timeout=2)
+        t0, t1 = self.window
+        inside = [x for x in self.fast if t0 is not None and t1 is not None and t0 <= x[0] <= t1]
+        if not inside:
+            return None
+        reasons = sorted(name for name, bit in self.NVML_REASONS if any(x[2] & bit for x in inside))
+        return {"sm_mhz": statistics.median(x[1] for x in inside), "sm_mhz_min": min(x[1] for x in inside),
+                "power_w_max": max(x[3] for x in inside), "reasons": reasons, "samples": len(inside)}
+
     def stop(self) -> dict:
+        fast = self._fast_summary()
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+            out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+            if fast is not None:
+                out.update(sm_mhz=fast["sm_mhz"], reasons=fast["reasons"], timed_region_nvml=fast)
+            return out
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -166,13 +218,21 @@ class ClockSampler:
             for name, flag in zip(names, parts[4:8]):
                 if flag.lower().startswith("active"):
                     reasons.add(name)
-        return {
+        out = {
             "sm_mhz": statistics.median(sm) if sm else None,
             "sm_max_mhz": max(smax) if smax else None,
             "power_w_max": max(power) if power else None,
             "reasons": sorted(reasons),
             "samples": len(sm),
         }
+        if fast is not None:
+            # the timed region's own samples decide the median clock and the
+            # reasons; the nvidia-smi samples (warm-up included) stay beside them
+            out["nvidia_smi"] = {k: out[k] for k in ("sm_mhz", "power_w_max", "reasons", "samples")}
+            out.update(sm_mhz=fast["sm_mhz"], power_w_max=fast["power_w_max"],
+                       reasons=sorted(set(fast["reasons"]) | reasons), samples=fast["samples"],
+                       sm_mhz_min=fast["sm_mhz_min"], source="NVML every 2 ms inside the timed region")
+        return out
 
 
 # ---------------------------------------------------------------- CPU baseline
@@ -456,11 +516,13 @@ def run_gpu_arm(args):
     barrier(world)
     torch.cuda.synchronize(device)
     launches_before = ctypes_count(lib)
+    sampler.mark_start()
     start.record(stream)
     for _ in range(args.steps):
         step()
     stop.record(stream)
     torch.cuda.synchronize(device)
+    sampler.mark_stop()
     launches_timed = ctypes_count(lib) - launches_before
     barrier(world)
     clocks = sampler.stop()
@@ -760,11 +822,13 @@ def run_comparison_arm(args):
     stream = torch.cuda.current_stream(device)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize(device)
+    sampler.mark_start()
     start.record(stream)
     for _ in range(args.steps):
         step()
     stop.record(stream)
     torch.cuda.synchronize(device)
+    sampler.mark_stop()
     clocks = sampler.stop()
     ms_step = start.elapsed_time(stop) / args.steps
     total_bytes = cfg.algorithmic_bytes(seqlens)
