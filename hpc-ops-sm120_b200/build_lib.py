@@ -64,18 +64,27 @@ def up_to_date(output: Path = OUTPUT, dependencies=None) -> bool:
     return all(dep.stat().st_mtime <= built for dep in (dependencies or DEPENDENCIES))
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and up_to_date():
-        return OUTPUT
-    cmd = [nvcc_path(), *NVCC_FLAGS, f"-I{INCLUDE}", f"-I{CSRC}", *map(str, SOURCES), "-o", str(OUTPUT) + ".tmp"]
+# Diagnostic build: the same library with the per-CTA timeline compiled in
+# (-DADB_TRACE), written outside the package (git-ignored _build/); used by
+# trace_decode.py.  The product never loads it.
+TRACE_OUTPUT = PACKAGE_DIR / "_build" / "trace" / "libattention_decode_b200.so"
+
+
+def build(force: bool = False, verbose: bool = False, trace: bool = False) -> Path:
+    output = TRACE_OUTPUT if trace else OUTPUT
+    if not force and up_to_date(output):
+        return output
+    output.parent.mkdir(parents=True, exist_ok=True)
+    extra = ["-DADB_TRACE"] if trace else []
+    cmd = [nvcc_path(), *NVCC_FLAGS, *extra, f"-I{INCLUDE}", f"-I{CSRC}", *map(str, SOURCES), "-o", str(output) + ".tmp"]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)
     result = subprocess.run(cmd, capture_output=not verbose, text=True)
     if result.returncode != 0:
         raise RuntimeError(f"nvcc failed ({result.returncode}):\n{result.stdout}\n{result.stderr}")
-    os.replace(str(OUTPUT) + ".tmp", OUTPUT)
-    return OUTPUT
+    os.replace(str(output) + ".tmp", output)
+    return output
 
 
 def build_torch_extension(force: bool = False, verbose: bool = False) -> Path:
@@ -116,7 +125,11 @@ def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--force", action="store_true")
     parser.add_argument("--verbose", action="store_true")
+    parser.add_argument("--trace", action="store_true", help="build only the diagnostic (per-CTA timeline) library")
     args = parser.parse_args()
+    if args.trace:
+        print(build(force=args.force, verbose=args.verbose, trace=True))
+        return 0
     print(build(force=args.force, verbose=args.verbose))
     print(build_torch_extension(force=args.force, verbose=args.verbose))
     return 0

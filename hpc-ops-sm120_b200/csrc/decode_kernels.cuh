@@ -1179,7 +1179,12 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
     }
     bar();
     const int64_t done = misc[46];  // 0: not complete; else 1 + thief segments
-    if (done) merge_pair(q, first, last, done - 1);
+    if (done) {
+      merge_pair(q, first, last, done - 1);
+      // the completing commit is the last to touch q's counter in this call:
+      // leave it zero for the next call
+      if (tid == 0) p.ws_done[q] = 0ull;
+    }
   };
 
   // Owner slots of pairs [q0, q1] whose tiles were all stolen: empty states,
@@ -1565,11 +1570,15 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   }
 
   // ------------------------------------------------------------ exit
-  // The last CTA to finish resets the scheduler header for the next call
-  // and, with a peer exchange, publishes this call's states to every rank:
-  // each CTA's stores (peer ones included) are released at GPU scope before
-  // it counts itself finished; the last CTA, having observed every count,
-  // fences at system scope and raises the flags, which releases them all.
+  // Without work stealing and without a peer exchange the only header state
+  // a call touches is the per-pair commit counters, which their completing
+  // commits zero (above), so a CTA just exits.  Otherwise the last CTA to
+  // finish resets the scheduler header for the next call and, with a peer
+  // exchange, publishes this call's states to every rank: each CTA's stores
+  // (peer ones included) are released at GPU scope before it counts itself
+  // finished; the last CTA, having observed every count, fences at system
+  // scope and raises the flags, which releases them all.  (The diagnostic
+  // build always counts, to number its launches.)
 #ifdef ADB_TRACE
   if (tid == 0 && c < kTraceCtas) {
     unsigned long long* r = g_adb_trace[g_adb_trace_launch & 1u][c];
@@ -1585,6 +1594,12 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
     r[12] = tr_cbusy;
   }
 #endif
+#ifdef ADB_TRACE
+  constexpr bool kCountAlways = true;
+#else
+  constexpr bool kCountAlways = false;
+#endif
+  if (!(kExchange || kCountAlways || steal)) return;
   __threadfence();
   bar();
   if (tid == 0) misc[46] = atomicAdd(p.ws_counters + 1, 1u) == static_cast<uint32_t>(nc - 1);
