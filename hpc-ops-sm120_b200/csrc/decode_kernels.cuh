@@ -610,9 +610,35 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
   // ------------------------------------------------------------ tile range
   // (varlen: computed after the wait below, from the sequence lengths)
   if (p.seqlens != nullptr) {
+    // A batch that fits the block: one load of the lengths and one scan give
+    // the total, the per-batch tile prefix (kept in shared memory) and the
+    // batches holding tiles t0 and t1 - 1.
+    if (B <= static_cast<int64_t>(blockDim.x)) {
+      if (tid == 0) misc[40] = misc[42] = -1;  // ordered by the scan's barriers
+      const int64_t x = tid < B ? Hkv * tiles_of(clamped_len(p, tid), TT) : 0;
+      int64_t total = 0;
+      const int64_t incl = block_inclusive_scan(x, misc, total);
+      nt_total = total;
+      have_table = true;
+      t0 = nt_total > 0 ? c * nt_total / nc : 0;
+      t1 = nt_total > 0 ? (c + 1) * nt_total / nc : 0;
+      const int64_t excl = incl - x;
+      if (tid < B) {
+        table[tid] = excl;
+        if (x > 0 && excl <= t0 && t0 < excl + x) {
+          misc[40] = tid;
+          misc[41] = excl;
+        }
+        if (x > 0 && excl <= t1 - 1 && t1 - 1 < excl + x) {
+          misc[42] = tid;
+          misc[43] = excl;
+        }
+      }
+      if (tid == 0) table[B] = total;
+    } else {
     // Pass 1: total tiles.  Pass 2: per-batch tile prefix (kept in shared
     // memory when the batch is small) and the batches holding tiles t0 and
-    // t1 - 1.  CTA 0 also writes the rows of empty sequences.
+    // t1 - 1.
     int64_t local = 0;
     for (int64_t b = tid; b < B; b += blockDim.x) local += Hkv * tiles_of(clamped_len(p, b), TT);
     int64_t total = 0;
@@ -648,12 +674,13 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
       }
       if (tid == 0 && have_table) table[B] = running;
     }
+    }
     __syncthreads();
     if (t0 < t1) {
       walk_locate(first_w, p, misc[40], misc[41], t0, TT);
       walk_locate(last_w, p, misc[42], misc[43], t1 - 1, TT);
     }
-    if (c == 0) {  // empty sequences: zero output rows / empty states
+    if (c == 0) {  // CTA 0 writes the rows of empty sequences (zero output / empty states)
       const int64_t Hq = Hkv * G;
       for (int64_t b = tid; b < B; b += blockDim.x) {
         if (clamped_len(p, b) != 0) continue;
