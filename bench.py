@@ -18,6 +18,11 @@ kernel stores its partial states into every rank's exchange buffer over
 NVLink and a merge kernel combines them on each rank, or with
 `--transport nccl` the states are all-gathered over NCCL: strong scaling).
 
+Timing: W warm-up steps and ~30 ms of further steps, a barrier and a
+synchronize, a ~0.5 ms device-side hold (so that the first timed steps are
+queued before they start), then K steps between CUDA events on the launching
+stream, a synchronize and a barrier; the max over ranks.
+
 `--impl reference` times the reference's CPU path on the host cores: the
 torch FP32 decode of attention_decode/reference.py:47-60 (restated with the
 same torch calls in oracle/reference_torch.py, all host threads) on the whole
@@ -233,6 +238,41 @@ class ClockSampler:
                        reasons=sorted(set(fast["reasons"]) | reasons), samples=fast["samples"],
                        sm_mhz_min=fast["sm_mhz_min"], source="NVML every 2 ms inside the timed region")
         return out
+
+
+# ---------------------------------------------------------------- timed region
+# The timed steps start behind a short device-side hold: torch's bounded
+# cycle-count sleep kernel (~0.5 ms at the B200's 1.965 GHz) on the timing
+# stream, launched after the barrier and synchronize and before the start
+# event.  By the time it ends the host has queued the first timed steps, so a
+# host-side pause while they are being launched (a thread switch, a driver
+# query) does not enter the device time; the timed region itself is K whole
+# steps on the device, unchanged.  The end-to-end pass has no hold.
+HOLD_CYCLES = 1_000_000
+
+
+def hold_queue():
+    torch.cuda._sleep(HOLD_CYCLES)
+
+
+def settle(step, device, warmup, world=1):
+    """Runs the W warm-up steps, then further steps for ~30 ms (SM clocks at
+    their loaded operating point right before the timing); returns how many
+    further steps ran.  Every rank runs the same count (sequence-sharded steps
+    exchange states with all ranks)."""
+    stream = torch.cuda.current_stream(device)
+    w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0.record(stream)
+    for _ in range(warmup):
+        step()
+    w1.record(stream)
+    torch.cuda.synchronize(device)
+    est_s = max_over_ranks(max(w0.elapsed_time(w1) * 1e-3 / warmup, 1e-6), world, device)
+    extra = int(min(5000, max(0, 0.03 / est_s - warmup)))
+    for _ in range(extra):
+        step()
+    torch.cuda.synchronize(device)
+    return extra
 
 
 # ---------------------------------------------------------------- CPU baseline
@@ -495,21 +535,8 @@ def run_gpu_arm(args):
     sampler.start()
     time.sleep(0.3)
     # Warm-up: the W steps asked for, then enough further steps to run the GPU
-    # for ~30 ms (SM clocks back at their loaded operating point), right
-    # before the timed steps.
-    w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    w0.record(stream)
-    for _ in range(args.warmup):
-        step()
-    w1.record(stream)
-    torch.cuda.synchronize(device)
-    # every rank runs the same number of steps (sequence-sharded steps
-    # exchange states with all ranks), so the count comes from one value
-    est_s = max_over_ranks(max(w0.elapsed_time(w1) * 1e-3 / args.warmup, 1e-6), world, device)
-    settle_steps = int(min(5000, max(0, 0.03 / est_s - args.warmup)))
-    for _ in range(settle_steps):
-        step()
-    torch.cuda.synchronize(device)
+    # for ~30 ms, right before the timed steps.
+    settle_steps = settle(step, device, args.warmup, world)
 
     # ---- device-timed region
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -517,6 +544,7 @@ def run_gpu_arm(args):
     torch.cuda.synchronize(device)
     launches_before = ctypes_count(lib)
     sampler.mark_start()
+    hold_queue()
     start.record(stream)
     for _ in range(args.steps):
         step()
@@ -660,6 +688,7 @@ def run_gpu_arm(args):
             "steps": args.steps,
             "warmup": args.warmup,
             "warmup_settle_steps": settle_steps,
+            "timed_start": f"behind a {HOLD_CYCLES}-cycle device-side hold (host launch jitter kept out)",
             "ms_per_step": ms_step,
             "us_per_step": ms_step * 1e3,
             "higher_is_better": True,
@@ -813,16 +842,16 @@ def run_comparison_arm(args):
         rotation[0] = (i + 1) % len(sets)
         return call(*sets[i])
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(device)
+    # the same warm-up, settle and hold as this library's arm
     sampler = ClockSampler(device)
     sampler.start()
     time.sleep(0.3)
+    settle_steps = settle(step, device, args.warmup)
     stream = torch.cuda.current_stream(device)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize(device)
     sampler.mark_start()
+    hold_queue()
     start.record(stream)
     for _ in range(args.steps):
         step()
@@ -840,6 +869,8 @@ def run_comparison_arm(args):
         "n_gpus": 1,
         "steps": args.steps,
         "warmup": args.warmup,
+        "warmup_settle_steps": settle_steps,
+        "timed_start": f"behind a {HOLD_CYCLES}-cycle device-side hold (host launch jitter kept out)",
         "ms_per_step": ms_step,
         "us_per_step": ms_step * 1e3,
         "higher_is_better": True,
