@@ -470,7 +470,7 @@ def run_gpu_arm(args):
             fp8_scales = (ks, vs)
             bytes_per_rank = (bytes_per_rank - 4 * cfg.batch * cfg.query_heads * cfg.head_dim) // 2 + \
                 4 * cfg.batch * cfg.query_heads * cfg.head_dim
-        sets, kv_total = rotation_sets(cfg, device, args.seed + 1009 * rank, (q, k, v))
+        sets, kv_total = rotation_sets(cfg, device, args.seed + 1009 * rank, (q, k, v), shard_index)
         if fp8_scales is not None:
             sets = [sets[0]] + [(qi, (ki.float() / fp8_scales[0]).to(torch.float8_e4m3fn),
                                  (vi.float() / fp8_scales[1]).to(torch.float8_e4m3fn)) for qi, ki, vi in sets[1:]]
@@ -644,8 +644,12 @@ def run_gpu_arm(args):
     if sequence_sharded:
         e2e_call = step_fn.with_query(q_dev)
     else:
-        def e2e_call():
-            return decode(q_dev, k, v, lens_dev)
+        e2e_rotation = [0]
+
+        def e2e_call():  # the K/V caches rotate as in the timed region
+            i = e2e_rotation[0]
+            e2e_rotation[0] = (i + 1) % n_sets
+            return decode(q_dev, sets[i][1], sets[i][2], lens_dev)
 
     def e2e_step():
         q_dev.copy_(q_host, non_blocking=True)
@@ -718,7 +722,8 @@ def run_gpu_arm(args):
                 "us_per_step": e2e_s * 1e6,
                 "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
-                "note": "per step: pinned H2D of Q, attention_decode() through the C ABI, D2H of O, host sync; the KV cache is resident decode state",
+                "note": "per step: pinned H2D of Q, attention_decode() through the C ABI, D2H of O, host sync; the KV cache is resident decode state"
+                        + ("" if sequence_sharded or n_sets == 1 else f" (rotating among the timed region's {n_sets} input sets)"),
             },
             "gpu_launches": launches_timed,
             "graph": graph_line,
@@ -737,17 +742,20 @@ def run_gpu_arm(args):
     return 0
 
 
-def rotation_sets(cfg, device, seed, first):
+def rotation_sets(cfg, device, seed, first, batch_slice=None):
     """Input sets that steps rotate among.  A KV cache smaller than twice the
     L2 would be served from L2 on the next step, so enough independent seeded
     sets are made that every step streams from HBM (the KV rotation of the
-    reference's bench_extreme.py:103-107).  Returns (sets, KV bytes per set)."""
+    reference's bench_extreme.py:103-107).  Every set has the shapes of
+    `first`: the same sequences of the batch (`batch_slice`, a rank's share
+    under strong scaling).  Returns (sets, KV bytes per set)."""
     q, k, v = first
     kv_total = 2 * k.numel() * k.element_size()
     n_sets = 1 if kv_total >= 2 * L2_BYTES else min(64, -(-2 * L2_BYTES // kv_total))
     sets = [(q, k, v)]
     for i in range(1, n_sets):
-        qi, ki, vi, _ = cfg.make_inputs(device, seed=seed + 7919 * i)
+        qi, ki, vi, _ = cfg.make_inputs(device, seed=seed + 7919 * i, batch_slice=batch_slice)
+        assert ki.shape == k.shape and qi.shape == q.shape
         sets.append((qi, ki, vi))
     return sets, kv_total
 

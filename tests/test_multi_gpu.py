@@ -2,7 +2,8 @@
 NVLink peer memory by the decode kernel itself -- merged in the same launch,
 or by a second kernel -- and through an NCCL all_gather; merged on every
 rank, eagerly and replayed from a CUDA graph) and
-batch sharding (no collective).  Needs at least two GPUs; ranks are spawned
+batch sharding (no collective), over 2, 4 and 8 ranks as far as the GPUs
+go (one GPU per rank).  Ranks are spawned
 processes, one per GPU, with a short process-group timeout so that a failure
 ends in an error, not a hang."""
 
@@ -90,12 +91,12 @@ def _worker(rank, world, port, results):
             pass
 
 
-def test_sequence_and_batch_sharding_over_nccl():
-    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
-        pytest.skip("needs at least two GPUs")
+@pytest.mark.parametrize("world", (2, 4, 8))
+def test_sequence_and_batch_sharding_over_nccl(world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
 
-    world = 2
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     port = _free_port()
