@@ -1650,10 +1650,11 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
 #endif
       if constexpr (kExchange) {
         ADB_TRACE_ONLY(const unsigned tr_l = (g_adb_trace_launch - 1u) & 255u; g_adb_launch_log[tr_l][2] = global_timer_ns();)
+        // release pattern: one system-scope fence, then the flags
         fence_acq_rel_sys();
         const uint32_t call = x_epoch(p) + 1u;
         for (int s = 0; s < p.x_world; ++s)
-          st_release_sys_u32(
+          st_relaxed_sys_u32(
               reinterpret_cast<uint32_t*>(p.x_base[s] + kXFlagsOffset) + p.x_rank, call);
         *reinterpret_cast<volatile uint32_t*>(p.x_base[p.x_rank] + kXEpochOffset) = call;
         ADB_TRACE_ONLY(g_adb_launch_log[tr_l][3] = global_timer_ns();)
@@ -1676,7 +1677,7 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
         const uint64_t start = global_timer_ns();
         for (int s = 0; s < p.x_world && ok; ++s) {
           // flags only grow; a rank one call ahead has already passed `call`
-          while (static_cast<int32_t>(ld_acquire_sys_u32(flags + s) - call) < 0) {
+          while (static_cast<int32_t>(ld_relaxed_sys_u32(flags + s) - call) < 0) {
             if (global_timer_ns() - start > p.x_timeout_ns) {
               ok = 0;
               atomicOr(&g_adb_error_flag, kErrPeerTimeout);
@@ -1685,6 +1686,7 @@ __global__ void __launch_bounds__(StreamCfg<D, kWarps, kMB, kStages, kTma>::kThr
             __nanosleep(32);
           }
         }
+        if (ok) fence_acq_rel_sys();  // acquire pattern: the flags, then one fence
         misc[54] = ok;
       }
       bar();
@@ -1775,7 +1777,7 @@ __global__ void __launch_bounds__(256)
     const uint64_t start = global_timer_ns();
     for (int s = 0; s < world && ok; ++s) {
       // Flags only grow; a rank one call ahead has already passed `call`.
-      while (static_cast<int32_t>(ld_acquire_sys_u32(flags + s) - call) < 0) {
+      while (static_cast<int32_t>(ld_relaxed_sys_u32(flags + s) - call) < 0) {
         if (global_timer_ns() - start > timeout_ns) {
           ok = 0;
           atomicOr(&g_adb_error_flag, kErrPeerTimeout);
@@ -1784,6 +1786,7 @@ __global__ void __launch_bounds__(256)
         __nanosleep(64);
       }
     }
+    if (ok) fence_acq_rel_sys();  // acquire pattern: the flags, then one fence
     ready = ok;
     ADB_TRACE_ONLY(if (blockIdx.x == 0) g_adb_merge_log[call & 255u][1] = global_timer_ns();)
   }

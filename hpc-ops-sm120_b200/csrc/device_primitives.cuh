@@ -223,10 +223,21 @@ __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
 
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue; it must call griddep_wait() before touching this grid's output.
-// System-scope release store / acquire load of a 32-bit flag: the flags that
-// ranks on other GPUs raise in this GPU's memory (and read in theirs).
-__device__ __forceinline__ void st_release_sys_u32(uint32_t* ptr, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+// System-scope strong (relaxed) store / load of a 32-bit flag: the flags that
+// ranks on other GPUs raise in this GPU's memory (and read in theirs).  With
+// fence_acq_rel_sys() they form the PTX memory model's release pattern (a
+// fence, then strong writes) and acquire pattern (strong reads, then a
+// fence), so a batch of flags costs one system-scope fence, not one per flag
+// as st.release.sys / ld.acquire.sys would (a system-scope fence waits for
+// every earlier write of the thread, peer writes over NVLink included).
+__device__ __forceinline__ void st_relaxed_sys_u32(uint32_t* ptr, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_relaxed_sys_u32(const uint32_t* ptr) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
 }
 
 // Release/acquire fence at system scope (orders this thread's, and by
@@ -234,12 +245,6 @@ __device__ __forceinline__ void st_release_sys_u32(uint32_t* ptr, uint32_t v) {
 // its later ones for observers on other GPUs); lighter than fence.sc.sys.
 __device__ __forceinline__ void fence_acq_rel_sys() {
   asm volatile("fence.acq_rel.sys;" ::: "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* ptr) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
-  return v;
 }
 
 __device__ __forceinline__ void griddep_launch_dependents() {
