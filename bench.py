@@ -252,7 +252,9 @@ HOLD_CYCLES = 1_000_000
 
 
 def hold_queue():
-    torch.cuda._sleep(HOLD_CYCLES)
+    sleep = getattr(torch.cuda, "_sleep", None)  # a private torch helper: skip the hold if it is gone
+    if sleep is not None:
+        sleep(HOLD_CYCLES)
 
 
 def settle(step, device, warmup, world=1):
