@@ -257,6 +257,12 @@ def hold_queue():
         sleep(HOLD_CYCLES)
 
 
+def timed_start_note():
+    if getattr(torch.cuda, "_sleep", None) is None:
+        return "right after the barrier and synchronize (no device-side hold available)"
+    return f"behind a {HOLD_CYCLES}-cycle device-side hold (host launch jitter kept out)"
+
+
 def settle(step, device, warmup, world=1):
     """Runs the W warm-up steps, then further steps for ~30 ms (SM clocks at
     their loaded operating point right before the timing); returns how many
@@ -694,7 +700,7 @@ def run_gpu_arm(args):
             "steps": args.steps,
             "warmup": args.warmup,
             "warmup_settle_steps": settle_steps,
-            "timed_start": f"behind a {HOLD_CYCLES}-cycle device-side hold (host launch jitter kept out)",
+            "timed_start": timed_start_note(),
             "ms_per_step": ms_step,
             "us_per_step": ms_step * 1e3,
             "higher_is_better": True,
@@ -880,7 +886,7 @@ def run_comparison_arm(args):
         "steps": args.steps,
         "warmup": args.warmup,
         "warmup_settle_steps": settle_steps,
-        "timed_start": f"behind a {HOLD_CYCLES}-cycle device-side hold (host launch jitter kept out)",
+        "timed_start": timed_start_note(),
         "ms_per_step": ms_step,
         "us_per_step": ms_step * 1e3,
         "higher_is_better": True,
